@@ -1,0 +1,56 @@
+"""Load-time symmetric int8 quantiser (host, numpy) and the dequantising row gather.
+
+These produce the operands of the int8 weight-only path; they run once at model
+load, never on the decode hot path, so they stay numpy on the host.
+
+Format (identical to quartz/quantize.py:26-48 so that the same fp32 weights give
+the same int8 bytes on both sides): ``w ~= q * scale`` with q int8 in [-127, 127]
+and one fp32 scale per group of ``G = K // ng`` consecutive input-dim elements
+(``group_size=None`` is one scale per output row). A group whose absmax is zero
+gets scale 1.0. Rounding is numpy's round-half-to-even.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+
+def quantize_symmetric(W: np.ndarray, group_size: int | None = None):
+    """(N, K) fp32 -> (q int8 (N, K) C-contiguous, scale fp32 (N, ng)).
+
+    Follows quartz/quantize.py:26-38: the scale is computed in float64 from the
+    fp32 absmax then cast to fp32; q = clip(round(W / scale), -127, 127), where
+    the division is fp32 / fp32 (numpy promotes nothing here).
+    """
+    W = np.ascontiguousarray(W, dtype=np.float32)
+    N, K = W.shape
+    G = group_size or K
+    if K % G != 0:
+        raise ValueError(f"group_size {G} does not divide input dim {K}")
+    ng = K // G
+    Wg = W.reshape(N, ng, G)
+    scale = (np.abs(Wg).max(axis=2) / 127.0).astype(np.float32)
+    scale[scale == 0] = 1.0
+    q = np.clip(np.round(Wg / scale[:, :, None]), -127, 127).astype(np.int8).reshape(N, K)
+    return np.ascontiguousarray(q), np.ascontiguousarray(scale)
+
+
+def dequantize_symmetric(q: np.ndarray, scale: np.ndarray, group_size: int | None = None) -> np.ndarray:
+    """fp32 (..., K) from int8 q (..., K) and scale (..., ng) (quartz/quantize.py:41-48)."""
+    shp = q.shape
+    K = shp[-1]
+    ng = scale.shape[-1]
+    G = K // ng
+    qf = q.astype(np.float32).reshape(*shp[:-1], ng, G)
+    return (qf * scale[..., None]).reshape(shp).astype(np.float32)
+
+
+def stack_gate_up(gate_q, gate_s, up_q, up_s):
+    """Stack gate rows over up rows -> ([2I, H] int8, [2I, ng] fp32).
+
+    The fused MLP reads intermediate unit n from rows n (gate) and n + I (up) of
+    one tensor, the layout quartz/quantize.py:95-96 builds.
+    """
+    gu_q = np.ascontiguousarray(np.concatenate([gate_q, up_q], axis=0))
+    gu_s = np.ascontiguousarray(np.concatenate([gate_s, up_s], axis=0))
+    return gu_q, gu_s

@@ -1,0 +1,94 @@
+"""Seeded synthetic workloads for the int8 weight-only path.
+
+Every input the tests and the benchmark use is drawn here from
+``np.random.default_rng(seed)`` so that any run can be reproduced from its seed.
+Two weight recipes exist because the reference uses two:
+
+* ``"f32"`` (the benchmark recipe): ``rng.standard_normal(shape, dtype=float32)
+  * float32(std)`` with std 0.02 -- the distribution of the lm_head / MLP
+  workloads (Qwen3-0.6B lm_head [151936, 1024]; MLP H=1024, I=3072 per layer).
+* ``"f64"`` (the recipe of quartz's own kernel tests, tests/test_kernels.py:25-26):
+  ``(rng.standard_normal(shape) * std).astype(float32)`` with std 0.05.
+
+Activations are N(0, 1) fp32 in both recipes.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import numpy as np
+
+from .quantize import quantize_symmetric, stack_gate_up
+
+# Qwen3-0.6B shapes (hidden 1024, MLP 3072, 28 layers, tied vocab 151936).
+LM_HEAD_N = 151936
+LM_HEAD_K = 1024
+MLP_H = 1024
+MLP_I = 3072
+MLP_LAYERS = 28
+MLP_LAYER_SEED0 = 1000
+
+
+def draw_weight(rng, shape, std=0.02, recipe="f32") -> np.ndarray:
+    if recipe == "f32":
+        return rng.standard_normal(shape, dtype=np.float32) * np.float32(std)
+    if recipe == "f64":
+        return (rng.standard_normal(shape) * std).astype(np.float32)
+    raise ValueError(f"unknown weight recipe {recipe!r}")
+
+
+def draw_act(rng, shape, recipe="f32") -> np.ndarray:
+    if recipe == "f32":
+        return rng.standard_normal(shape, dtype=np.float32)
+    return rng.standard_normal(shape).astype(np.float32)
+
+
+@dataclass
+class GemvCase:
+    q: np.ndarray       # int8 [N, K]
+    scale: np.ndarray   # fp32 [N, ng]
+    x: np.ndarray       # fp32 [M, K]
+
+
+def gemv_case(N, K, M=1, *, seed=0, group_size=None, std=0.02, recipe="f32") -> GemvCase:
+    """Weights first, then activations, from one rng (the lm_head recipe when
+    N=151936, K=1024, seed 0)."""
+    rng = np.random.default_rng(seed)
+    W = draw_weight(rng, (N, K), std, recipe)
+    q, s = quantize_symmetric(W, group_size)
+    del W
+    x = draw_act(rng, (M, K), recipe)
+    return GemvCase(q, s, x)
+
+
+@dataclass
+class MlpCase:
+    gu_q: np.ndarray    # int8 [2I, H]  (gate rows, then up rows)
+    gu_s: np.ndarray    # fp32 [2I, ng]
+    down_q: np.ndarray  # int8 [H, I]
+    down_s: np.ndarray  # fp32 [H, ng_d]
+    x: np.ndarray       # fp32 [M, H]
+
+
+def mlp_case(H, I, M=1, *, seed=0, group_size=None, std=0.02, recipe="f32") -> MlpCase:
+    """gate, up, down, then x from one rng. Layer l of the Qwen3-0.6B MLP body
+    workload is ``mlp_case(1024, 3072, seed=1000 + l)``."""
+    rng = np.random.default_rng(seed)
+    gq, gs = quantize_symmetric(draw_weight(rng, (I, H), std, recipe), group_size)
+    uq, us = quantize_symmetric(draw_weight(rng, (I, H), std, recipe), group_size)
+    dq, ds = quantize_symmetric(draw_weight(rng, (H, I), std, recipe), group_size)
+    x = draw_act(rng, (M, H), recipe)
+    gu_q, gu_s = stack_gate_up(gq, gs, uq, us)
+    return MlpCase(gu_q, gu_s, dq, ds, x)
+
+
+def gemv_algorithmic_bytes(N, K, ng=1, M=1) -> int:
+    """int8 weights + fp32 scales + fp32 activations in + fp32 outputs, each once."""
+    return N * K + 4 * N * ng + 4 * M * K + 4 * M * N
+
+
+def mlp_algorithmic_bytes(H, I, ng=1, ngd=1, M=1) -> int:
+    """gate|up and down int8 + their scales + x in + out; the [I] intermediate
+    stays on chip/L2 and is not counted."""
+    return 2 * I * H + H * I + 4 * (2 * I * ng + H * ngd) + 4 * M * H * 2
