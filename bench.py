@@ -1,0 +1,346 @@
+"""Benchmark of the int8 weight-only path on B200.
+
+Default workload (the one the headline metric is quoted on): the standalone
+fused int8 GEMV at the Qwen3-0.6B lm_head shape -- q int8 [151936, 1024] from
+per-row absmax quantisation of N(0, 0.02) fp32 draws (seed 0), x fp32 [1024]
+~ N(0, 1), y = scale * (q . x) fp32 [151936].
+
+A step is one GEMV over the whole lm_head. Steps rotate over several copies of
+the weights (each 155.6 MB, larger than the 126 MB L2) so no step reads weights
+the previous step left in L2.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line. `value` is the device-timed whole-job HBM GB/s of
+algorithmic bytes (int8 weights + fp32 scales + x + y, each once); `e2e` is the
+same metric through the public numpy API (host x in, host y out, copies
+included); `cpu_baseline` is the CPU oracle (a C/OpenMP restatement of the
+reference's Numba kernel) on this host's cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+import numpy as np
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+
+from quartz_b200.workloads import (LM_HEAD_K, LM_HEAD_N, gemv_algorithmic_bytes,  # noqa: E402
+                                   gemv_case)
+
+METRIC = "int8 GEMV achieved HBM GB/s (% of B200 peak); all-int8 decode tok/s"
+UNIT = "GB/s"
+WORKLOAD = "qwen3-0.6b lm_head int8 GEMV [151936x1024], M=1, per-row scale"
+
+
+def _peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def _cpu_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+# ---------------------------------------------------------------------------
+# clocks sampled while the timed region runs
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int, period_ms: int = 20):
+        self.gpu = gpu_index
+        self.period = period_ms
+        self.proc = None
+        self.path = Path(os.environ.get("TMPDIR", "/tmp")) / f"qz_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", f"-lms", str(self.period)],
+                stdout=self.f, stderr=subprocess.DEVNULL)
+            time.sleep(0.3)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.1)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self) -> dict:
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                rows.append(dict(sm=float(parts[1]), smax=float(parts[2]),
+                                 power=float(parts[3]) if parts[3] not in ("[N/A]", "") else None,
+                                 hw=parts[5], hwt=parts[6], swt=parts[7], swp=parts[8]))
+            except ValueError:
+                continue
+        try:
+            self.path.unlink()
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        reasons = set()
+        for r in rows:
+            if r["hw"] == "Active":
+                reasons.add("hw_slowdown")
+            if r["hwt"] == "Active":
+                reasons.add("hw_thermal_slowdown")
+            if r["swt"] == "Active":
+                reasons.add("sw_thermal_slowdown")
+            if r["swp"] == "Active":
+                reasons.add("sw_power_cap")
+        powers = [r["power"] for r in rows if r["power"] is not None]
+        return {"sm_mhz": statistics.median(r["sm"] for r in rows),
+                "sm_max_mhz": max(r["smax"] for r in rows),
+                "reasons": sorted(reasons),
+                "samples": len(rows),
+                "power_w_max": max(powers) if powers else None}
+
+
+# ---------------------------------------------------------------------------
+# CPU side (oracle = C/OpenMP restatement of quartz/kernels/int8.py:24-38)
+# ---------------------------------------------------------------------------
+def cpu_gemv_gbs(case, reps: int, threads: int | None = None):
+    import oracle
+    if threads:
+        oracle.set_threads(threads)
+    y = np.empty(case.q.shape[0], np.float32)
+    x = np.ascontiguousarray(case.x[0])
+    oracle.w8a32_gemv(case.q, case.scale, x, y)          # warm
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        oracle.w8a32_gemv(case.q, case.scale, x, y)
+        ts.append(time.perf_counter() - t0)
+    nbytes = gemv_algorithmic_bytes(*case.q.shape, case.scale.shape[1])
+    med = statistics.median(ts)
+    return nbytes / med / 1e9, med, oracle.threads(), oracle.load().isa
+
+
+def run_reference(args) -> dict:
+    """--impl reference: the CPU oracle on all host threads, K timed steps."""
+    case = gemv_case(LM_HEAD_N, LM_HEAD_K, seed=0)
+    import oracle
+    oracle.set_threads(_cpu_cores())
+    y = np.empty(LM_HEAD_N, np.float32)
+    x = np.ascontiguousarray(case.x[0])
+    for _ in range(args.warmup):
+        oracle.w8a32_gemv(case.q, case.scale, x, y)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.w8a32_gemv(case.q, case.scale, x, y)
+    dt = (time.perf_counter() - t0) / max(1, args.steps)
+    nbytes = gemv_algorithmic_bytes(LM_HEAD_N, LM_HEAD_K)
+    gbs = nbytes / dt / 1e9
+    return {
+        "metric": METRIC, "value": round(gbs, 3), "unit": UNIT, "impl": "reference",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "int8 weights, fp32 accumulate", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "seed": 0},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": UNIT, "cores": oracle.threads(),
+                         "kind": "port",
+                         "sample": f"full lm_head GEMV per step, {args.steps} steps "
+                                   f"({oracle.load().isa})"},
+        "e2e": {"value": round(gbs, 3), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+
+
+# ---------------------------------------------------------------------------
+# GPU side
+# ---------------------------------------------------------------------------
+def run_ours(args) -> dict:
+    import torch
+    from quartz_b200 import device as qdev
+    from quartz_b200 import kernels as qk
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda:0")
+    qdev.ensure_device(dev)
+    qdev.status(clear=True)
+
+    case = gemv_case(LM_HEAD_N, LM_HEAD_K, seed=0)
+    N, K = case.q.shape
+    nbytes = gemv_algorithmic_bytes(N, K)
+    copies = args.copies
+    qs = [torch.from_numpy(case.q).to(dev) for _ in range(copies)]
+    ss = [torch.from_numpy(case.scale).to(dev) for _ in range(copies)]
+    x = torch.from_numpy(case.x[0]).to(dev)
+    ys = [torch.empty(N, dtype=torch.float32, device=dev) for _ in range(copies)]
+
+    def step(i):
+        j = i % copies
+        qdev.gemv(qs[j], ss[j], x, ys[j])
+
+    # correctness gate before timing: copy 0 against the CPU oracle
+    import oracle
+    y_ref = np.empty(N, np.float32)
+    oracle.w8a32_gemv(case.q, case.scale, case.x[0], y_ref)
+    step(0)
+    torch.cuda.synchronize()
+    rel = float(np.abs(ys[0].cpu().numpy() - y_ref).max() / np.abs(y_ref).max())
+    if rel > 1e-4:
+        raise SystemExit(f"parity check failed before timing: rel err {rel:.3e}")
+
+    stream = torch.cuda.current_stream()
+    use_graph = not args.no_graph
+    if use_graph:
+        # One graph holds `chunk` consecutive steps; replays are enqueued back to back.
+        chunk = min(args.steps, 256)
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(stream)
+        with torch.cuda.stream(s):
+            step(0)
+        stream.wait_stream(s)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g):
+            for i in range(chunk):
+                step(i)
+        torch.cuda.synchronize()
+
+    def run(n):
+        if use_graph:
+            full, rem = divmod(n, chunk)
+            for _ in range(full):
+                g.replay()
+            for i in range(rem):
+                step(i)
+        else:
+            for i in range(n):
+                step(i)
+
+    run(args.warmup)
+    torch.cuda.synchronize()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        torch.cuda.synchronize()
+        start.record(stream)
+        run(args.steps)
+        end.record(stream)
+        torch.cuda.synchronize()
+    ms = start.elapsed_time(end) / args.steps
+    qdev.check_status()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    peak, peak_kind = _peaks()
+
+    # e2e: public numpy API, host x in and host y out every step
+    e2e = None
+    if not args.no_e2e:
+        qnp = [case.q.copy() for _ in range(copies)]
+        snp = [case.scale.copy() for _ in range(copies)]
+        xh = np.ascontiguousarray(case.x[0])
+        yh = np.empty(N, np.float32)
+        for j in range(copies):
+            qk.w8a32_gemv(qnp[j], snp[j], xh, yh)          # first use uploads the weights
+        for i in range(args.warmup):
+            qk.w8a32_gemv(qnp[i % copies], snp[i % copies], xh, yh)
+        esteps = max(1, min(args.steps, args.e2e_steps))
+        t0 = time.perf_counter()
+        for i in range(esteps):
+            qk.w8a32_gemv(qnp[i % copies], snp[i % copies], xh, yh)
+        et = (time.perf_counter() - t0) / esteps
+        rel_e = float(np.abs(yh - y_ref).max() / np.abs(y_ref).max())
+        if rel_e > 1e-4:
+            raise SystemExit(f"e2e parity failed: rel err {rel_e:.3e}")
+        e2e = {"value": round(nbytes / et / 1e9, 2), "unit": UNIT,
+               "h2d_bytes_per_step": int(xh.nbytes), "d2h_bytes_per_step": int(yh.nbytes),
+               "ms_per_step": round(et * 1e3, 4), "steps": esteps,
+               "note": "numpy w8a32_gemv; int8 weights resident after first use"}
+
+    cpu = None
+    if not args.no_cpu:
+        cgbs, cmed, cthreads, isa = cpu_gemv_gbs(case, reps=args.cpu_reps, threads=_cpu_cores())
+        cpu = {"value": round(cgbs, 3), "unit": UNIT, "cores": cthreads, "kind": "port",
+               "sample": f"full lm_head GEMV, median of {args.cpu_reps} calls "
+                         f"({cmed * 1e3:.3f} ms each, {isa})"}
+
+    traffic = None
+    tpath = REPO / "profiles" / "gemv_lm_head_traffic.json"
+    if tpath.exists():
+        traffic = json.loads(tpath.read_text()).get("dram_bytes_per_launch")
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    return {
+        "metric": METRIC, "value": round(gbs, 2), "unit": UNIT, "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 weights, fp32 accumulate", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "seed": 0, "weight_copies": copies,
+                   "l2": f"inputs larger than L2: {copies} rotating weight copies of "
+                         f"{N * K / 1e6:.1f} MB", "graph": use_graph,
+                   "bytes_per_step": nbytes},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": UNIT,
+                     "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                     "traffic": traffic},
+        "e2e": e2e,
+        "cpu_baseline": cpu,
+        "clocks": clk.summary(),
+        "gpu_launches": args.steps,
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=4000)
+    ap.add_argument("--warmup", type=int, default=100)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--copies", type=int, default=3)
+    ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=500)
+    ap.add_argument("--cpu-reps", type=int, default=30)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+
+    rank = int(os.environ.get("RANK", "0"))
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        print(json.dumps(run_reference(args)))
+        return
+    if args.gpus != 1:
+        raise SystemExit("multi-GPU bench not implemented yet")
+    print(json.dumps(run_ours(args)))
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,108 @@
+/*
+ * quartz_b200.h -- C ABI of the B200 (sm_100a) int8 weight-only matmul path.
+ *
+ * Replaces the native kernels behind quartz's `quartz.kernels` package (a Numba
+ * JIT, CPU only in the reference). Pointers are DEVICE pointers; host<->device
+ * copies and the device-resident weight cache live in the Python layer
+ * (quartz_b200.kernels), which keeps the reference's numpy signatures.
+ *
+ * Conventions
+ *   - Every entry point returns an int status (QZ_OK == 0). On failure,
+ *     qz_last_error() returns a message for the calling thread. No C++
+ *     exception crosses this boundary.
+ *   - All work is stream-ordered on `stream` (a cudaStream_t; NULL = the
+ *     legacy default stream). Nothing here synchronises except qz_sync().
+ *   - Layouts are C-contiguous. q is int8 [N, K]; scale is fp32 [N, ng] with
+ *     K % ng == 0 and group size G = K / ng (ng == 1: one scale per row).
+ *   - Any N, K, M >= 0 is accepted. The streaming kernels run when q is
+ *     16-byte aligned, K % 16 == 0 and G % 16 == 0; other shapes take a generic
+ *     kernel with the same results (within fp32 reassociation).
+ *   - Kernels that wait (mbarrier stages, the fused MLP's grid barrier) give
+ *     up after about one second, record the failure in a device status word
+ *     and return; qz_device_status() reads it.
+ */
+#ifndef QUARTZ_B200_H_
+#define QUARTZ_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  QZ_OK = 0,
+  QZ_ERR_INVALID = 1,     /* bad argument: shape, null pointer, group tiling */
+  QZ_ERR_CUDA = 2,        /* a CUDA runtime call failed */
+  QZ_ERR_UNSUPPORTED = 3, /* device is not sm_100 / missing capability */
+};
+
+/* Library version, (major << 16) | (minor << 8) | patch. */
+int qz_version(void);
+
+/* Select `device`, check it is an sm_100 part, and prepare kernel attributes.
+ * Optional: the first call on a device does the same. */
+int qz_init(int device);
+
+/* Copy the calling thread's last error message into buf (NUL-terminated,
+ * truncated to len). Returns the full message length. */
+int qz_last_error(char* buf, size_t len);
+
+/*
+ * y[n] = sum_g scale[n, g] * sum_{j < G} x[g*G + j] * q[n, g*G + j]  (+ residual[n])
+ * Replaces w8a32_gemv and w8a32_gemv_serial
+ * (quartz/kernels/int8.py:24-38 and :48-63): the reference's size-based
+ * serial/parallel choice (int8.py:45,101-105) becomes a launch-shape choice
+ * here. residual may be NULL.
+ */
+int qz_gemv_w8(const int8_t* q, const float* scale, int64_t ng, const float* x, float* y,
+               int64_t N, int64_t K, const float* residual, void* stream);
+
+/*
+ * Y[m, n] = the same reduction for each of M rows of X [M, K]  (+ residual[m, n])
+ * Replaces w8a32_gemm (quartz/kernels/int8.py:66-87). Y is [M, N]; residual,
+ * if not NULL, is [M, N]. M == 1 runs the GEMV.
+ */
+int qz_gemm_w8(const int8_t* q, const float* scale, int64_t ng, const float* X, float* Y,
+               int64_t M, int64_t N, int64_t K, const float* residual, void* stream);
+
+/*
+ * out[h] = sum down[h, :] * abuf * down_s  (+ residual[h]),
+ *   abuf[n] = silu(gate_n . x) * (up_n . x)     (silu with unclipped exp)
+ * Replaces fused_mlp_decode (quartz/kernels/fused.py:27-65).
+ *   gu_q [2I, H] int8 (gate rows 0..I-1, up rows I..2I-1), gu_s [2I, ng];
+ *   x [H]; down_q [H, I] int8, down_s [H, ngd]; abuf [I] (written, as in the
+ *   reference); out [H]; residual [H] or NULL.
+ * sync_ws: qz_mlp_workspace_bytes() bytes of device memory, zeroed once before
+ * its first use; the kernel leaves it ready for the next call. Calls that
+ * share one sync_ws must not overlap on the GPU.
+ */
+int qz_fused_mlp_decode(const int8_t* gu_q, const float* gu_s, int64_t ng, const float* x,
+                        const int8_t* down_q, const float* down_s, int64_t ngd, float* abuf,
+                        float* out, const float* residual, int64_t H, int64_t I,
+                        uint32_t* sync_ws, void* stream);
+
+/* Bytes of device workspace qz_fused_mlp_decode needs for its grid barrier. */
+int qz_mlp_workspace_bytes(void);
+
+/*
+ * a[m, i] = silu(gu[m, i]) * gu[m, I + i], exponent clipped to [-88, 88].
+ * The elementwise step of the M > 1 MLP (quartz/quantize.py:112-114 with
+ * quartz/ops.py:35-37). gu is [M, 2I], a is [M, I].
+ */
+int qz_silu_mul(const float* gu, float* a, int64_t M, int64_t I, void* stream);
+
+/* Read the device status word of the current device into words[0..3]
+ * ({error bits, first error site, block of first error, error count}); when
+ * clear != 0 reset it to zero afterwards. Synchronises the device. */
+int qz_device_status(uint32_t* words, int clear);
+
+/* cudaStreamSynchronize(stream) with the error mapped to a status. */
+int qz_sync(void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* QUARTZ_B200_H_ */
