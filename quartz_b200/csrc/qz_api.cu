@@ -30,6 +30,11 @@ int fail(int code, const std::string& msg) {
 
 constexpr int kMaxDevices = 64;
 
+// Rows per group of the streaming kernels: 4 for tall matrices, 1 when a tall
+// grouping would leave SMs idle.
+constexpr int kTallRows = 4;
+constexpr int kMinBlocks = 3;   // launch bound: CTAs per SM the register budget allows
+
 struct DeviceInfo {
   bool ready = false;
   int sms = 0;
@@ -39,6 +44,41 @@ struct DeviceInfo {
 
 DeviceInfo g_dev[kMaxDevices];
 std::mutex g_dev_mu;
+
+template <class F>
+cudaError_t allow_smem(F* fn, int bytes) {
+  return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+}
+
+template <int R>
+cudaError_t allow_gemv_variants(int smem) {
+  cudaError_t e = cudaSuccess;
+  auto set = [&](auto fn) { if (e == cudaSuccess) e = allow_smem(fn, smem); };
+  set(qz::gemv_kernel<R, true, qz::K1K, kMinBlocks>);
+  set(qz::gemv_kernel<R, true, qz::KFULL, kMinBlocks>);
+  set(qz::gemv_kernel<R, true, qz::KANY, kMinBlocks>);
+  set(qz::gemv_kernel<R, false, qz::K1K, kMinBlocks>);
+  set(qz::gemv_kernel<R, false, qz::KFULL, kMinBlocks>);
+  set(qz::gemv_kernel<R, false, qz::KANY, kMinBlocks>);
+  return e;
+}
+
+template <int R>
+cudaError_t allow_mlp_variants(int smem) {
+  cudaError_t e = cudaSuccess;
+  auto set = [&](auto fn) { if (e == cudaSuccess) e = allow_smem(fn, smem); };
+  set(qz::fused_mlp_kernel<R, true, qz::KFULL, qz::KFULL, kMinBlocks>);
+  set(qz::fused_mlp_kernel<R, true, qz::KANY, qz::KANY, kMinBlocks>);
+  set(qz::fused_mlp_kernel<R, false, qz::KFULL, qz::KFULL, kMinBlocks>);
+  set(qz::fused_mlp_kernel<R, false, qz::KANY, qz::KANY, kMinBlocks>);
+  return e;
+}
+
+int kmode(int64_t K) {
+  if (K == qz::kSegBytes) return qz::K1K;
+  if (K % qz::kSegBytes == 0) return qz::KFULL;
+  return qz::KANY;
+}
 
 int device_info(DeviceInfo** out) {
   int dev = 0;
@@ -59,14 +99,10 @@ int device_info(DeviceInfo** out) {
       d.coop = p.cooperativeLaunch;
       // Leave room for the kernels' few bytes of static shared memory.
       const int smem = d.smem_optin - 256;
-      QZ_CUDA(cudaFuncSetAttribute(qz::gemv_stream_kernel<true>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      QZ_CUDA(cudaFuncSetAttribute(qz::gemv_stream_kernel<false>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      QZ_CUDA(cudaFuncSetAttribute(qz::fused_mlp_kernel<true>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-      QZ_CUDA(cudaFuncSetAttribute(qz::fused_mlp_kernel<false>,
-                                   cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+      QZ_CUDA(allow_gemv_variants<kTallRows>(smem));
+      QZ_CUDA(allow_gemv_variants<1>(smem));
+      QZ_CUDA(allow_mlp_variants<kTallRows>(smem));
+      QZ_CUDA(allow_mlp_variants<2>(smem));
       d.ready = true;
     }
   }
@@ -75,18 +111,6 @@ int device_info(DeviceInfo** out) {
 }
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
-
-// Stages that fit next to an x region of xbytes; 0 when fewer than 2 fit.
-int stream_stages(const DeviceInfo& d, int64_t kmax) {
-  const int64_t avail = static_cast<int64_t>(d.smem_optin) - qz::kSmemHeader -
-                        qz::stream_x_bytes(kmax) - 256 /* static shared */;
-  if (avail < 2 * qz::kStageBytes) return 0;
-  return static_cast<int>(std::min<int64_t>(qz::kMaxStages, avail / qz::kStageBytes));
-}
-
-int stream_smem(int64_t kmax, int nstages) {
-  return qz::kSmemHeader + qz::stream_x_bytes(kmax) + nstages * qz::kStageBytes;
-}
 
 int check_weights(const int8_t* q, const float* scale, int64_t ng, int64_t N, int64_t K,
                   const char* what) {
@@ -111,24 +135,96 @@ int launch_generic_gemm(const DeviceInfo& d, const int8_t* q, const float* scale
   return QZ_OK;
 }
 
+// Launch `fn` with programmatic stream serialisation (and optionally as a
+// cooperative grid). Kernels launched this way issue their first weight
+// copies before griddepcontrol.wait, overlapping the previous kernel's tail.
+template <class... Args>
+int launch_ex(void (*fn)(Args...), int grid, int smem, cudaStream_t st, bool cooperative,
+              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(qz::kThreads);
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  if (cooperative) {
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+  } else {
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  QZ_CUDA(cudaLaunchKernelEx(&cfg, fn, args...));
+  return QZ_OK;
+}
+
+// CTAs of `fn` that fit on one SM with `smem` bytes of dynamic shared memory.
+template <class F>
+int blocks_per_sm(F* fn, int smem, int* out) {
+  int nb = 0;
+  QZ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fn, qz::kThreads, smem));
+  *out = nb;
+  return QZ_OK;
+}
+
+template <int R, bool PER_ROW, int KM>
+int launch_gemv(const DeviceInfo& d, const qz::GemvArgs& a, cudaStream_t st) {
+  auto fn = qz::gemv_kernel<R, PER_ROW, KM, kMinBlocks>;
+  const int smem = KM == qz::K1K ? qz::ring_bytes(R) : qz::stream_smem_bytes(R, a.K);
+  int nb = 0;
+  if (int rc = blocks_per_sm(fn, smem, &nb)) return rc;
+  if (nb < 1) return fail(QZ_ERR_UNSUPPORTED, "gemv: shared memory does not fit");
+  const int64_t want = qz::cdiv(a.N, int64_t(R) * qz::kWarps);
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, int64_t(d.sms) * nb)));
+  return launch_ex(fn, grid, smem, st, false, a);
+}
+
+template <int R, bool PER_ROW>
+int launch_gemv_k(const DeviceInfo& d, const qz::GemvArgs& a, cudaStream_t st) {
+  switch (kmode(a.K)) {
+    case qz::K1K: return launch_gemv<R, PER_ROW, qz::K1K>(d, a, st);
+    case qz::KFULL: return launch_gemv<R, PER_ROW, qz::KFULL>(d, a, st);
+    default: return launch_gemv<R, PER_ROW, qz::KANY>(d, a, st);
+  }
+}
+
 int gemv_impl(const int8_t* q, const float* scale, int64_t ng, const float* x, float* y,
               int64_t N, int64_t K, const float* residual, cudaStream_t st) {
   DeviceInfo* d = nullptr;
   if (int rc = device_info(&d)) return rc;
   const int64_t G = K / ng;
-  const int nst = stream_stages(*d, K);
-  const bool fast = K > 0 && K % 16 == 0 && G % 16 == 0 && aligned16(q) && nst >= 2;
+  const bool fits = qz::stream_smem_bytes(kTallRows, K) <= d->smem_optin - 256;
+  const bool fast = K > 0 && K % 16 == 0 && G % 16 == 0 && aligned16(q) && fits;
   if (!fast) return launch_generic_gemm(*d, q, scale, ng, x, y, residual, 1, N, K, st);
-  qz::GemvArgs a{q, scale, x, y, residual, N, K, ng, nst};
-  const int64_t n_rg = qz::cdiv(N, qz::kRW);
-  const int grid = static_cast<int>(std::min<int64_t>(n_rg, d->sms));
-  const int smem = stream_smem(K, nst);
+  const qz::GemvArgs a{q, scale, x, y, residual, N, K, ng};
+  // Tall grouping unless it would leave SMs without a CTA.
+  const bool tall = qz::cdiv(N, int64_t(kTallRows) * qz::kWarps) >= d->sms;
   if (ng == 1)
-    qz::gemv_stream_kernel<true><<<grid, qz::kThreads, smem, st>>>(a);
-  else
-    qz::gemv_stream_kernel<false><<<grid, qz::kThreads, smem, st>>>(a);
-  QZ_CUDA(cudaGetLastError());
-  return QZ_OK;
+    return tall ? launch_gemv_k<kTallRows, true>(*d, a, st) : launch_gemv_k<1, true>(*d, a, st);
+  return tall ? launch_gemv_k<kTallRows, false>(*d, a, st) : launch_gemv_k<1, false>(*d, a, st);
+}
+
+template <int R, bool PER_ROW, int KM>
+int launch_mlp(const DeviceInfo& d, const qz::MlpArgs& a, cudaStream_t st) {
+  auto fn = qz::fused_mlp_kernel<R, PER_ROW, KM, KM, kMinBlocks>;
+  const int smem = qz::stream_smem_bytes(R, std::max(a.H, a.I));
+  int nb = 0;
+  if (int rc = blocks_per_sm(fn, smem, &nb)) return rc;
+  if (nb < 1) return fail(QZ_ERR_UNSUPPORTED, "fused mlp: shared memory does not fit");
+  const int64_t want = std::max(qz::cdiv(a.I, int64_t(R / 2) * qz::kWarps),
+                                qz::cdiv(a.H, int64_t(R) * qz::kWarps));
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, int64_t(d.sms) * nb)));
+  return launch_ex(fn, grid, smem, st, true, a);
+}
+
+template <int R, bool PER_ROW>
+int launch_mlp_k(const DeviceInfo& d, const qz::MlpArgs& a, cudaStream_t st) {
+  // Both phases without partial items when H and I are whole KB multiples.
+  if (a.H % qz::kSegBytes == 0 && a.I % qz::kSegBytes == 0)
+    return launch_mlp<R, PER_ROW, qz::KFULL>(d, a, st);
+  return launch_mlp<R, PER_ROW, qz::KANY>(d, a, st);
 }
 
 }  // namespace
@@ -188,9 +284,9 @@ int qz_fused_mlp_decode(const int8_t* gu_q, const float* gu_s, int64_t ng, const
   DeviceInfo* d = nullptr;
   if (int rc = device_info(&d)) return rc;
   const int64_t kmax = std::max(H, I);
-  const int nst = stream_stages(*d, kmax);
+  const bool fits = qz::stream_smem_bytes(kTallRows, kmax) <= d->smem_optin - 256;
   const bool fast = I > 0 && H % 16 == 0 && I % 16 == 0 && (H / ng) % 16 == 0 &&
-                    (I / ngd) % 16 == 0 && aligned16(gu_q) && aligned16(down_q) && nst >= 2 &&
+                    (I / ngd) % 16 == 0 && aligned16(gu_q) && aligned16(down_q) && fits &&
                     sync_ws != nullptr && d->coop;
   if (!fast) {
     // Two launches: gate/up + SiLU into abuf, then the down GEMV.
@@ -202,16 +298,13 @@ int qz_fused_mlp_decode(const int8_t* gu_q, const float* gu_s, int64_t ng, const
     }
     return launch_generic_gemm(*d, down_q, down_s, ngd, abuf, out, residual, 1, H, I, st);
   }
-  qz::MlpArgs a{gu_q, gu_s, x, down_q, down_s, abuf, out, residual, sync_ws, H, I, ng, ngd, nst};
-  const int64_t work = std::max(qz::cdiv(I, qz::kRW / 2), qz::cdiv(H, qz::kRW));
-  const int grid = static_cast<int>(std::min<int64_t>(work, d->sms));
-  const int smem = stream_smem(kmax, nst);
-  void* args[] = {&a};
-  const void* fn = (ng == 1 && ngd == 1)
-                       ? reinterpret_cast<const void*>(qz::fused_mlp_kernel<true>)
-                       : reinterpret_cast<const void*>(qz::fused_mlp_kernel<false>);
-  QZ_CUDA(cudaLaunchCooperativeKernel(fn, dim3(grid), dim3(qz::kThreads), args, smem, st));
-  return QZ_OK;
+  const qz::MlpArgs a{gu_q, gu_s, x, down_q, down_s, abuf, out, residual, sync_ws, H, I, ng, ngd};
+  const bool per_row = ng == 1 && ngd == 1;
+  // Tall groups (2 units = 4 rows) unless too few units to fill the SMs.
+  const bool tall = qz::cdiv(I, int64_t(kTallRows / 2) * qz::kWarps) >= d->sms;
+  if (per_row)
+    return tall ? launch_mlp_k<kTallRows, true>(*d, a, st) : launch_mlp_k<2, true>(*d, a, st);
+  return tall ? launch_mlp_k<kTallRows, false>(*d, a, st) : launch_mlp_k<2, false>(*d, a, st);
 }
 
 int qz_silu_mul(const float* gu, float* a, int64_t M, int64_t I, void* stream) {

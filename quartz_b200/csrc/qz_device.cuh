@@ -115,6 +115,33 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       : "memory");
 }
 
+// Per-stage position tags. mbarrier parity waits only tell the current phase
+// from the previous one, so a consumer that may run ahead of the ring first
+// waits until the producer has published (st.release) the position it wants.
+__device__ __forceinline__ void st_release_shared(uint32_t addr, uint32_t v) {
+  asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_shared(uint32_t addr) {
+  uint32_t v;
+  asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(addr) : "memory");
+  return v;
+}
+
+// Wait until the word at `addr` equals `want`; false after kWaitLimitNs.
+__device__ __forceinline__ bool wait_tag(uint32_t addr, uint32_t want) {
+  if (ld_acquire_shared(addr) == want) return true;
+  const unsigned long long t0 = globaltimer();
+  while (true) {
+#pragma unroll 1
+    for (int i = 0; i < 16; ++i) {
+      __nanosleep(32);
+      if (ld_acquire_shared(addr) == want) return true;
+    }
+    if (globaltimer() - t0 > kWaitLimitNs) return false;
+  }
+}
+
 // Named barrier over the first `nthreads` threads of the CTA (id != 0).
 __device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t nthreads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
@@ -179,7 +206,7 @@ __device__ __forceinline__ void dot4_acc(uint32_t w, f2_t x01, f2_t x23, f2_t& a
 }
 
 // One 16-byte chunk of weights against 16 activations held as 8 fp32 pairs.
-__device__ __forceinline__ void dot16_acc(const uint4& q, const f2_t (&x)[8], f2_t& acc) {
+__device__ __forceinline__ void dot16_acc(const uint4& q, const f2_t* x, f2_t& acc) {
   dot4_acc(q.x, x[0], x[1], acc);
   dot4_acc(q.y, x[2], x[3], acc);
   dot4_acc(q.z, x[4], x[5], acc);

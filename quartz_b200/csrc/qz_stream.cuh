@@ -1,41 +1,55 @@
 // qz_stream.cuh -- HBM-streaming int8 weight-only kernels for M = 1 (decode).
 //
-//   gemv_stream_kernel   y[n] = sum_g scale[n,g] * sum_{k in g} x[k] * q[n,k]  (+ residual[n])
-//                        (quartz/kernels/int8.py:24-38 and its serial twin 48-63)
-//   fused_mlp_kernel     out = down(silu(gate.x) * (up.x))  (+ residual)
-//                        (quartz/kernels/fused.py:27-65)
+//   gemv_kernel       y[n] = sum_g scale[n,g] * sum_{k in g} x[k] * q[n,k]  (+ residual[n])
+//                     (quartz/kernels/int8.py:24-38 and its serial twin 48-63)
+//   fused_mlp_kernel  out = down(silu(gate.x) * (up.x))  (+ residual)
+//                     (quartz/kernels/fused.py:27-65)
 //
-// Shape of both kernels: one persistent CTA per SM, 16 consumer warps and one
-// producer warp. The producer's elected lane streams the CTA's slice of the
-// weight matrix through a ring of shared-memory stages with 1-D bulk copies
-// (cp.async.bulk, the TMA engine) that complete on per-stage mbarriers. A
-// stage is a "row group": 8 weight rows x up to 1024 bytes of K. Each consumer
-// warp owns whole row groups: lane l takes 16-byte chunks l, l+32, ... of the
-// 8 rows, widens int8 -> fp32 in registers (qz_device.cuh), and accumulates
-// fp32 pairs; activations sit in shared memory in a bank-conflict-free layout
-// and are read once per chunk for all 8 rows. One transposed butterfly
-// reduces the 8 row sums; the per-row scale, SiLU gate and residual are fused
-// into that epilogue. The fp32 weight array is never formed.
+// Structure (chosen by measurement on B200):
+//   * every warp owns a balanced, contiguous range of weight rows and walks it
+//     in row groups of R rows; a group is cut along K into items of at most
+//     1 KB per row;
+//   * each lane streams its own 16-byte chunks of an item into a private slot
+//     of the warp's shared-memory ring (cp.async.cg, kDepth items deep: bytes
+//     in flight cost no registers) and later reads back exactly those bytes,
+//     so no intra-warp synchronisation is needed;
+//   * activations are staged once per CTA in shared memory in a
+//     bank-conflict-free [word][chunk] layout;
+//   * int8 -> fp32 widening in registers (qz_device.cuh), packed f32x2 FMAs,
+//     one transposed butterfly per group; scale, residual and SiLU gate are
+//     fused into the epilogue. No fp32 weight array is ever formed;
+//   * weights do not depend on the previous kernel in the stream, so a launch
+//     issues its first weight copies before it waits on the programmatic
+//     dependency (griddepcontrol.wait) and touches activations or outputs.
 #pragma once
 
 #include "qz_device.cuh"
 
 namespace qz {
 
-constexpr int kRW = 8;                          // weight rows per row group / stage
-constexpr int kConsumerWarps = 16;
-constexpr int kThreads = (kConsumerWarps + 1) * 32;
-constexpr int kSeg = 1024;                      // K bytes per stage row
-constexpr int kMaxStages = 32;
-constexpr int kStageBytes = kRW * kSeg;
-constexpr int kSmemHeader = 2 * kMaxStages * 8 + 128;  // barriers (+ flags), 128-aligned
+constexpr int kWarps = 8;                  // warps per CTA
+constexpr int kThreads = kWarps * 32;
+constexpr int kSegBytes = 1024;            // K bytes per row per item (32 lanes x 2 chunks)
+constexpr int kDepth = 2;                  // items in flight per warp ring
+
+// How K relates to the 1 KB item width, fixed at compile time so the hot loop
+// carries no bounds checks in the common cases.
+enum KMode : int {
+  K1K = 0,    // K == 1024: one item per row group, activations in registers
+  KFULL = 1,  // K % 1024 == 0: every item is a full 1 KB per row
+  KANY = 2,   // K % 16 == 0: the last item of a row may be partial
+};
 
 __host__ __device__ constexpr int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 __host__ __device__ constexpr int64_t min64(int64_t a, int64_t b) { return a < b ? a : b; }
 
-// Layout of dynamic shared memory: [full[32] | empty[32] | flags][x: xfloats][stages]
+// Shared memory: [x: kmax floats, 128-aligned][rings: kWarps * kDepth * R * kSegBytes]
 __host__ __device__ inline int stream_x_bytes(int64_t kmax) {
   return static_cast<int>(((kmax * 4 + 127) / 128) * 128);
+}
+__host__ __device__ constexpr int ring_bytes(int R) { return kWarps * kDepth * R * kSegBytes; }
+__host__ __device__ inline int stream_smem_bytes(int R, int64_t kmax) {
+  return stream_x_bytes(kmax) + ring_bytes(R);
 }
 
 struct GemvArgs {
@@ -45,7 +59,6 @@ struct GemvArgs {
   float* y;               // [N]
   const float* residual;  // [N] or null
   int64_t N, K, ng;
-  int nstages;
 };
 
 struct MlpArgs {
@@ -54,19 +67,39 @@ struct MlpArgs {
   const float* x;         // [H]
   const int8_t* down_q;   // [H, I]
   const float* down_s;    // [H, ngd]
-  float* abuf;            // [I] intermediate, global (read back after the grid barrier)
+  float* abuf;            // [I] intermediate (global; read back after the grid barrier)
   float* out;             // [H]
   const float* residual;  // [H] or null
   unsigned int* sync_ws;  // grid barrier words {count, generation}, zero at first use
   int64_t H, I, ng, ngd;
-  int nstages;
 };
 
-// Stage the K activations into shared memory as float4 blocks ordered
-// [word j4][chunk c] so that lane-consecutive chunks hit consecutive banks.
+// ---------------------------------------------------------------------------
+// cp.async ring + programmatic dependent launch
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// Wait until the grids this one depends on have completed and their memory is
+// visible (a no-op without a programmatic dependency).
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// Allow the next kernel in the stream to begin launching; it still waits for
+// this grid's completion before it reads anything this grid writes.
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Stage K activations into shared memory as float4 blocks ordered [word j4][chunk c].
 // COHERENT: the source was written earlier in this kernel by other CTAs (the
-// fused MLP's intermediate, read after the grid barrier), so it is read from
-// L2 (ld.global.cg), never through the non-coherent path.
+// fused MLP's intermediate, read after the grid barrier): read it from L2
+// (ld.global.cg), never through the non-coherent path.
 template <bool COHERENT = false>
 __device__ __forceinline__ void stage_x(float* xs, const float* x, int64_t K, int tid, int nthr) {
   const int64_t nch = K / 16;
@@ -76,134 +109,134 @@ __device__ __forceinline__ void stage_x(float* xs, const float* x, int64_t K, in
   }
 }
 
-// Load the 16 activations of global chunk gc as 8 fp32 pairs.
-__device__ __forceinline__ void load_x16(uint32_t xs_base, int64_t nch, int64_t gc, f2_t (&xv)[8]) {
+// Activations of global chunk gc as 8 fp32 pairs.
+__device__ __forceinline__ void load_x16(const uint8_t* xs, int64_t nch, int64_t gc,
+                                         f2_t (&xv)[8]) {
 #pragma unroll
-  for (int j4 = 0; j4 < 4; ++j4)
-    lds_f2x2(xs_base + static_cast<uint32_t>((j4 * nch + gc) * 16), xv[2 * j4], xv[2 * j4 + 1]);
+  for (int j4 = 0; j4 < 4; ++j4) {
+    const ulonglong2 p = *reinterpret_cast<const ulonglong2*>(xs + (j4 * nch + gc) * 16);
+    xv[2 * j4] = p.x;
+    xv[2 * j4 + 1] = p.y;
+  }
 }
 
 // ---------------------------------------------------------------------------
-// Producer: issue the bulk copies for stage positions [0, total) in order.
-// `rows_of(pos)` is the bitmask of stage rows that exist at position pos;
-// `src_of(pos, r, k0)` is the global address of stage row r at K offset k0.
-// Rows are packed in the stage at r * seglen. With a single K segment, runs
-// of rows that are adjacent in global memory go out as one copy.
-// Returns the number of positions issued.
+// A warp's walk over one weight matrix: row groups [0, ngrp) of R rows, each
+// cut into nseg K-segments; item (g, seg) is number g * nseg + seg of the walk.
+// Items occupy consecutive ring positions starting at pos0, i.e. ring slot
+// (pos0 + item) % kDepth, so two walks can share one ring back to back.
+// Cursors advance item by item without divisions.
 // ---------------------------------------------------------------------------
-template <class RowsFn, class SrcFn>
-__device__ __forceinline__ int produce(uint32_t full0, uint32_t empty0, uint32_t stage0,
-                                       int nstages, int total, int nseg, int64_t K,
-                                       RowsFn rows_of, SrcFn src_of, unsigned int site) {
-  const uint64_t pol = l2_evict_first_policy();
-  int pos = 0;
-  for (; pos < total; ++pos) {
-    const int s = pos % nstages;
-    const int use = pos / nstages;
-    if (use > 0 && !mbar_wait(empty0 + 8 * s, (use - 1) & 1)) {
-      report_error(ERR_WAIT_EMPTY, site);
-      break;
-    }
-    const int seg = pos % nseg;
-    const int64_t k0 = static_cast<int64_t>(seg) * kSeg;
-    const int sl = static_cast<int>(min64(kSeg, K - k0));
-    const uint32_t dst = stage0 + s * kStageBytes;
-    const uint32_t mask = rows_of(pos);
-    const uint32_t bytes = static_cast<uint32_t>(__popc(mask)) * sl;
-    mbar_arrive_expect_tx(full0 + 8 * s, bytes);
-    if (nseg == 1) {
-      // Whole rows: coalesce runs of adjacent valid rows into one copy.
-      int r = 0;
-      while (r < kRW) {
-        if (!((mask >> r) & 1u)) { ++r; continue; }
-        const char* base = static_cast<const char*>(src_of(pos, r, 0));
-        int run = 1;
-        while (r + run < kRW && ((mask >> (r + run)) & 1u) &&
-               static_cast<const char*>(src_of(pos, r + run, 0)) == base + run * K)
-          ++run;
-        bulk_g2s(dst + r * sl, base, static_cast<uint32_t>(run * sl), full0 + 8 * s, pol);
-        r += run;
+template <int R>
+struct Walk {
+  const int8_t* q;
+  int64_t K;        // row length in bytes
+  int64_t ngrp;
+  int nseg;
+  int64_t pos0;     // ring position of item 0
+  __device__ int64_t items() const { return ngrp * nseg; }
+};
+
+struct Cursor {
+  int64_t g;        // row group
+  int seg;          // K segment
+  int slot;         // ring slot
+  __device__ void next(int nseg) {
+    if (++seg == nseg) { seg = 0; ++g; }
+    slot = slot + 1 == kDepth ? 0 : slot + 1;
+  }
+};
+
+template <int R>
+__device__ __forceinline__ Cursor cursor_at(const Walk<R>& w, int64_t it) {
+  Cursor c;
+  c.g = it / w.nseg;
+  c.seg = static_cast<int>(it - c.g * w.nseg);
+  c.slot = static_cast<int>((w.pos0 + it) % kDepth);
+  return c;
+}
+
+// Issue the copies of the item at cursor c (if it exists), then commit one
+// cp.async group. rowfn(g, r) -> global row index, or -1 when absent.
+template <int R, int KM, class RowFn>
+__device__ __forceinline__ void issue_item(const Walk<R>& w, uint32_t ring, const Cursor& c,
+                                           int lane, RowFn rowfn) {
+  if (c.g < w.ngrp) {
+    const int64_t k0 = KM == K1K ? 0 : static_cast<int64_t>(c.seg) * kSegBytes;
+    const int64_t slen = KM == KANY ? min64(kSegBytes, w.K - k0) : kSegBytes;
+    const uint32_t slot = ring + static_cast<uint32_t>(c.slot * R * kSegBytes);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int64_t row = rowfn(c.g, r);
+      if (row >= 0) {
+        const int8_t* src = w.q + row * w.K + k0;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          const int ch = lane + 32 * j;
+          if (KM != KANY || ch * 16 < slen)
+            cp_async16(slot + r * kSegBytes + ch * 16, src + ch * 16);
+        }
       }
-    } else {
-#pragma unroll 1
-      for (int r = 0; r < kRW; ++r)
-        if ((mask >> r) & 1u)
-          bulk_g2s(dst + r * sl, src_of(pos, r, k0), static_cast<uint32_t>(sl), full0 + 8 * s, pol);
     }
   }
-  return pos;
+  cp_async_commit();
 }
 
-// Wait (bounded) until every copy issued for positions [issued - nstages, issued)
-// has landed, so that no bulk copy is still writing this CTA's shared memory
-// when it exits. On the normal path these phases completed long ago.
-__device__ __forceinline__ void drain(uint32_t full0, int nstages, int issued, unsigned int site) {
-  for (int pos = max(0, issued - nstages); pos < issued; ++pos)
-    if (!mbar_wait(full0 + 8 * (pos % nstages), (pos / nstages) & 1)) {
-      report_error(ERR_DRAIN, site);
-      return;
-    }
-}
-
-// ---------------------------------------------------------------------------
-// Consumer core: one row group (8 rows) over all nseg segments starting at
-// stage position pos0. PER_ROW (ng == 1): fp32 pair accumulators, scale applied
-// by the caller. Otherwise each 16-element chunk's sum is weighted by the scale
-// of its group (G % 16 == 0 so a chunk never straddles two groups).
-// Returns false if a wait gave up.
-// ---------------------------------------------------------------------------
-template <bool PER_ROW, class ScaleFn>
-__device__ __forceinline__ bool consume_group(uint32_t full0, uint32_t empty0, uint32_t stage0,
-                                              uint32_t xs_base, int nstages, int pos0, int nseg,
-                                              int64_t K, int64_t G, int lane, ScaleFn scale_of,
-                                              float (&v)[8], unsigned int site) {
-  const int64_t nch_all = K / 16;
-  f2_t acc[kRW];
-  float accs[kRW];
+// Accumulate the (landed) item at cursor c into the per-row accumulators.
+// PER_ROW: one scale per row, applied by the caller; acc holds fp32 pairs.
+// Otherwise each 16-element chunk's dot is weighted by its group's scale
+// scale_of(g, r, group) (G % 16 == 0, so a chunk never straddles groups).
+// K1K: xr holds this lane's 2 chunks of activations (loaded once per walk).
+template <int R, bool PER_ROW, int KM, class ScaleFn>
+__device__ __forceinline__ void accumulate_item(const Walk<R>& w, const uint8_t* ring,
+                                                const uint8_t* xs, const f2_t (&xr)[2][8],
+                                                const Cursor& c, int lane, int64_t G,
+                                                f2_t (&acc)[R], float (&accs)[R],
+                                                ScaleFn scale_of) {
+  const int64_t k0 = KM == K1K ? 0 : static_cast<int64_t>(c.seg) * kSegBytes;
+  const int64_t slen = KM == KANY ? min64(kSegBytes, w.K - k0) : kSegBytes;
+  const uint8_t* slot = ring + c.slot * R * kSegBytes;
 #pragma unroll
-  for (int r = 0; r < kRW; ++r) { acc[r] = 0ull; accs[r] = 0.f; }
-  bool ok = true;
-  for (int seg = 0; seg < nseg; ++seg) {
-    const int pos = pos0 + seg;
-    const int s = pos % nstages;
-    ok = mbar_wait(full0 + 8 * s, (pos / nstages) & 1);
-    ok = __all_sync(0xffffffffu, ok);
-    if (!ok) {
-      if (lane == 0) report_error(ERR_WAIT_FULL, site);
-      break;
-    }
-    const int64_t k0 = static_cast<int64_t>(seg) * kSeg;
-    const int sl = static_cast<int>(min64(kSeg, K - k0));
-    const int nch = sl / 16;
-    const int64_t c0 = k0 / 16;
-    const uint32_t st = stage0 + s * kStageBytes;
-#pragma unroll 1
-    for (int c = lane; c < nch; c += 32) {
-      f2_t xv[8];
-      load_x16(xs_base, nch_all, c0 + c, xv);
+  for (int j = 0; j < 2; ++j) {
+    const int ch = lane + 32 * j;
+    if (KM != KANY || ch * 16 < slen) {
+      const int64_t gc = k0 / 16 + ch;
+      f2_t xl[8];
+      if constexpr (KM != K1K) load_x16(xs, w.K / 16, gc, xl);
+      const f2_t* xv = KM == K1K ? xr[j] : xl;
       if (PER_ROW) {
+        uint4 qv[R];
 #pragma unroll
-        for (int r = 0; r < kRW; ++r) {
-          const uint4 qv = lds128(st + r * sl + c * 16);
-          dot16_acc(qv, xv, acc[r]);
-        }
+        for (int r = 0; r < R; ++r)
+          qv[r] = *reinterpret_cast<const uint4*>(slot + r * kSegBytes + ch * 16);
+#pragma unroll
+        for (int r = 0; r < R; ++r) dot16_acc(qv[r], xv, acc[r]);
       } else {
-        const int64_t g = ((c0 + c) * 16) / G;
+        const int64_t grp = (gc * 16) / G;
 #pragma unroll
-        for (int r = 0; r < kRW; ++r) {
-          const uint4 qv = lds128(st + r * sl + c * 16);
+        for (int r = 0; r < R; ++r) {
+          const uint4 qv = *reinterpret_cast<const uint4*>(slot + r * kSegBytes + ch * 16);
           f2_t d = 0ull;
           dot16_acc(qv, xv, d);
           const float2 p = f2_unpack(d);
-          accs[r] = fmaf(p.x + p.y, scale_of(r, g), accs[r]);
+          accs[r] = fmaf(p.x + p.y, scale_of(c.g, r, grp), accs[r]);
         }
       }
     }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(empty0 + 8 * s);
   }
+}
+
+// Sum the R per-lane row values over the warp. R > 1: afterwards row
+// r = (lane >> 2) & 7 is complete on the lanes with that index. R == 1: every
+// lane holds the sum.
+template <int R, bool PER_ROW>
+__device__ __forceinline__ float reduce_rows(const f2_t (&acc)[R], const float (&accs)[R],
+                                             int lane) {
+  float v[8];
 #pragma unroll
-  for (int r = 0; r < kRW; ++r) {
+  for (int r = 0; r < 8; ++r) v[r] = 0.f;
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
     if (PER_ROW) {
       const float2 p = f2_unpack(acc[r]);
       v[r] = p.x + p.y;
@@ -211,91 +244,147 @@ __device__ __forceinline__ bool consume_group(uint32_t full0, uint32_t empty0, u
       v[r] = accs[r];
     }
   }
-  return ok;
+  if (R == 1) {
+    float s = v[0];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    return s;
+  }
+  return warp_reduce8(v, lane);
+}
+
+// The row (within its group) that this lane holds after reduce_rows, or -1.
+template <int R>
+__device__ __forceinline__ int reduced_row(int lane) {
+  if (R == 1) return lane == 0 ? 0 : -1;
+  const int r = (lane >> 2) & 7;
+  return ((lane & 3) == 0 && r < R) ? r : -1;
+}
+
+// This lane's two chunks of activations (K == 1024) as fp32 pairs, straight
+// from global memory (16-byte aligned x) or, unaligned, element by element.
+__device__ __forceinline__ void load_x_regs(const float* x, int lane, f2_t (&xr)[2][8]) {
+  const bool al = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
+#pragma unroll
+  for (int j = 0; j < 2; ++j) {
+    const float* xp = x + (lane + 32 * j) * 16;
+#pragma unroll
+    for (int t = 0; t < 4; ++t) {
+      float4 v;
+      if (al) {
+        v = *reinterpret_cast<const float4*>(xp + 4 * t);
+      } else {
+        v = make_float4(xp[4 * t], xp[4 * t + 1], xp[4 * t + 2], xp[4 * t + 3]);
+      }
+      xr[j][2 * t] = f2_pack(__float_as_uint(v.x), __float_as_uint(v.y));
+      xr[j][2 * t + 1] = f2_pack(__float_as_uint(v.z), __float_as_uint(v.w));
+    }
+  }
+}
+
+// One walk through the ring. Before the call, the positions of items
+// 0 .. kDepth-2 have been issued (committed as one group each). Each step
+// issues the item kDepth-1 ahead (past the end: `beyond()` issues the next
+// walk's item or an empty group), waits for the current item and accumulates
+// it; at a group's last segment `done(g, sum)` runs on every lane (sum is
+// meaningful on the lanes reduced_row<R>() names).
+// K1K walks take their activations from `xg` (global) into registers;
+// the others read the CTA's staged copy `xs` item by item.
+template <int R, bool PER_ROW, int KM, class RowFn, class ScaleFn, class BeyondFn, class DoneFn>
+__device__ __forceinline__ void walk(const Walk<R>& w, uint32_t ring_s, const uint8_t* ring,
+                                     const uint8_t* xs, const float* xg, int lane, int64_t G,
+                                     RowFn rowfn, ScaleFn scale_of, BeyondFn beyond,
+                                     DoneFn done) {
+  static_assert(kDepth == 2, "the look-ahead cursor below assumes a two-slot ring");
+  f2_t xr[2][8];
+  if constexpr (KM == K1K) load_x_regs(xg, lane, xr);
+  f2_t acc[R];
+  float accs[R];
+  Cursor cur = cursor_at(w, 0);
+  Cursor ahead = cur;
+  ahead.next(w.nseg);
+  for (; cur.g < w.ngrp; cur.next(w.nseg), ahead.next(w.nseg)) {
+    if (ahead.g < w.ngrp)
+      issue_item<R, KM>(w, ring_s, ahead, lane, rowfn);
+    else
+      beyond();
+    cp_async_wait<kDepth - 1>();
+    if (cur.seg == 0) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) { acc[r] = 0ull; accs[r] = 0.f; }
+    }
+    accumulate_item<R, PER_ROW, KM>(w, ring, xs, xr, cur, lane, G, acc, accs, scale_of);
+    if (KM == K1K || cur.seg == w.nseg - 1) done(cur.g, reduce_rows<R, PER_ROW>(acc, accs, lane));
+  }
+}
+
+// Balanced split of [0, n) into `parts`: the range [b, e) of part p.
+__device__ __forceinline__ void split_range(int64_t n, int64_t parts, int64_t p, int64_t& b,
+                                            int64_t& e) {
+  b = n * p / parts;
+  e = n * (p + 1) / parts;
 }
 
 // ---------------------------------------------------------------------------
 // GEMV
 // ---------------------------------------------------------------------------
-template <bool PER_ROW>
-__global__ void __launch_bounds__(kThreads, 1) gemv_stream_kernel(const GemvArgs a) {
+template <int R, bool PER_ROW, int KM, int MINB>
+__global__ void __launch_bounds__(kThreads, MINB) gemv_kernel(const GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t full0 = smem_u32(smem), empty0 = full0 + 8 * kMaxStages;
-  float* xs = reinterpret_cast<float*>(smem + kSmemHeader);
-  const uint32_t xs_base = smem_u32(xs);
-  const uint32_t stage0 = xs_base + stream_x_bytes(a.K);
+  float* xs = reinterpret_cast<float*>(smem);
+  const uint8_t* ring =
+      smem + (KM == K1K ? 0 : stream_x_bytes(a.K)) + warp * kDepth * R * kSegBytes;
+  const uint32_t ring_s = smem_u32(ring);
 
-  const int64_t n_rg = cdiv(a.N, kRW);
-  const int64_t rg_begin = n_rg * blockIdx.x / gridDim.x;
-  const int64_t rg_end = n_rg * (blockIdx.x + 1) / gridDim.x;
-  const int n_loc = static_cast<int>(rg_end - rg_begin);
-  const int nseg = static_cast<int>(cdiv(a.K, kSeg));
+  const int64_t nw = static_cast<int64_t>(gridDim.x) * kWarps;
+  const int64_t wg = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
+  int64_t r0, r1;
+  split_range(a.N, nw, wg, r0, r1);
+  const Walk<R> w{a.q, a.K, cdiv(r1 - r0, R), static_cast<int>(cdiv(a.K, kSegBytes)), 0};
+  auto rowfn = [&](int64_t g, int r) -> int64_t {
+    const int64_t row = r0 + g * R + r;
+    return row < r1 ? row : -1;
+  };
+  issue_item<R, KM>(w, ring_s, cursor_at(w, 0), lane, rowfn);
+  pdl_trigger();
+  pdl_wait();
+  if constexpr (KM != K1K) {
+    stage_x(xs, a.x, a.K, tid, kThreads);
+    __syncthreads();
+  }
+
   const int64_t G = a.K / a.ng;
-
-  if (tid == 0) {
-    for (int s = 0; s < a.nstages; ++s) {
-      mbar_init(full0 + 8 * s, 1);
-      mbar_init(empty0 + 8 * s, 1);
-    }
-    fence_mbar_init();
-  }
-  if (warp < kConsumerWarps) stage_x(xs, a.x, a.K, tid, kConsumerWarps * 32);
-  __syncthreads();
-
-  if (warp == kConsumerWarps) {
-    if (lane == 0) {
-      const int8_t* q = a.q;
-      const int64_t N = a.N, K = a.K;
-      auto rows_of = [&](int pos) -> uint32_t {
-        const int64_t row0 = (rg_begin + pos / nseg) * kRW;
-        const int64_t rows = min64(kRW, N - row0);
-        return (1u << rows) - 1u;
-      };
-      auto src_of = [&](int pos, int r, int64_t k0) -> const void* {
-        const int64_t row = (rg_begin + pos / nseg) * kRW + r;
-        return q + row * K + k0;
-      };
-      const int issued = produce(full0, empty0, stage0, a.nstages, n_loc * nseg, nseg, K, rows_of,
-                                 src_of, 0x100u);
-      drain(full0, a.nstages, issued, 0x101u);
-    }
-    return;
-  }
-
-  for (int rgl = warp; rgl < n_loc; rgl += kConsumerWarps) {
-    const int64_t row0 = (rg_begin + rgl) * kRW;
-    auto scale_of = [&](int r, int64_t g) -> float {
-      const int64_t row = row0 + r;
-      return row < a.N ? __ldg(a.scale + row * a.ng + g) : 0.f;
-    };
-    float v[8];
-    if (!consume_group<PER_ROW>(full0, empty0, stage0, xs_base, a.nstages, rgl * nseg, nseg, a.K,
-                                G, lane, scale_of, v, 0x102u))
-      return;
-    const float sum = warp_reduce8(v, lane);
-    const int64_t row = row0 + ((lane >> 2) & 7);
-    if ((lane & 3) == 0 && row < a.N) {
-      float o = PER_ROW ? sum * __ldg(a.scale + row) : sum;
+  auto scale_of = [&](int64_t g, int r, int64_t grp) -> float {
+    const int64_t row = r0 + g * R + r;
+    return row < r1 ? __ldg(a.scale + row * a.ng + grp) : 0.f;
+  };
+  auto done = [&](int64_t g, float s) {
+    const int r = reduced_row<R>(lane);
+    const int64_t row = r0 + g * R + r;
+    if (r >= 0 && row < r1) {
+      float o = PER_ROW ? s * __ldg(a.scale + row) : s;
       if (a.residual) o += a.residual[row];
       a.y[row] = o;
     }
-  }
+  };
+  auto beyond = [&]() { cp_async_commit(); };
+  walk<R, PER_ROW, KM>(w, ring_s, ring, reinterpret_cast<const uint8_t*>(xs), a.x, lane, G, rowfn,
+                       scale_of, beyond, done);
+  cp_async_wait<0>();
 }
 
 // ---------------------------------------------------------------------------
-// Fused MLP (M = 1). Phase 1: a row group is 4 intermediate units = 4 gate rows
-// (stage rows 0-3) + the matching 4 up rows (stage rows 4-7); the epilogue
+// Fused MLP (M = 1). Phase 1 walks "unit groups" of R/2 intermediate units,
+// stored as R/2 gate rows followed by the matching R/2 up rows; its epilogue
 // writes abuf[n] = silu(gate_n . x) * (up_n . x). A grid-wide barrier (bounded
-// spin on a generation counter; the launch is cooperative so every CTA is
+// spin on a generation counter; the launch is cooperative so all CTAs are
 // resident) separates it from phase 2, the down GEMV over abuf with the
-// residual fused. The producer does not wait at the barrier: it keeps
-// streaming this CTA's down rows into free stages, so phase 2's weights are
-// already in flight while phase 1 drains.
+// residual fused. Phase 2's first weight copies go out before the barrier.
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ bool grid_barrier(unsigned int* ws, int tid, unsigned int site) {
   __shared__ unsigned int s_fail;
-  named_bar_sync(1, kConsumerWarps * 32);
+  __syncthreads();
   if (tid == 0) {
     s_fail = 0u;
     __threadfence();
@@ -313,155 +402,108 @@ __device__ __forceinline__ bool grid_barrier(unsigned int* ws, int tid, unsigned
           s_fail = 1u;
           break;
         }
+        __nanosleep(32);
       }
     }
   }
-  named_bar_sync(1, kConsumerWarps * 32);
+  __syncthreads();
   return s_fail == 0u;
 }
 
-template <bool PER_ROW>
-__global__ void __launch_bounds__(kThreads, 1) fused_mlp_kernel(const MlpArgs a) {
+template <int R, bool PER_ROW, int KM1, int KM2, int MINB>
+__global__ void __launch_bounds__(kThreads, MINB) fused_mlp_kernel(const MlpArgs a) {
+  static_assert(kDepth == 2, "phase hand-over below assumes a two-slot ring");
+  static_assert(R % 2 == 0, "a unit group holds R/2 gate rows and R/2 up rows");
+  constexpr int U = R / 2;
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const uint32_t full0 = smem_u32(smem), empty0 = full0 + 8 * kMaxStages;
-  float* xs = reinterpret_cast<float*>(smem + kSmemHeader);
-  const uint32_t xs_base = smem_u32(xs);
-  const uint32_t stage0 = xs_base + stream_x_bytes(a.H > a.I ? a.H : a.I);
-
   const int64_t H = a.H, I = a.I;
-  constexpr int kUnits = kRW / 2;
-  const int64_t n_ug = cdiv(I, kUnits);
-  const int64_t ug_begin = n_ug * blockIdx.x / gridDim.x;
-  const int n1 = static_cast<int>(n_ug * (blockIdx.x + 1) / gridDim.x - ug_begin);
-  const int64_t n_rg = cdiv(H, kRW);
-  const int64_t rg_begin = n_rg * blockIdx.x / gridDim.x;
-  const int n2 = static_cast<int>(n_rg * (blockIdx.x + 1) / gridDim.x - rg_begin);
-  const int nseg1 = static_cast<int>(cdiv(H, kSeg));
-  const int nseg2 = static_cast<int>(cdiv(I, kSeg));
-  const int base2 = n1 * nseg1;
-  const int64_t G1 = H / a.ng, G2 = I / a.ngd;
+  float* xs = reinterpret_cast<float*>(smem);
+  const uint8_t* ring = smem + stream_x_bytes(H > I ? H : I) + warp * kDepth * R * kSegBytes;
+  const uint32_t ring_s = smem_u32(ring);
 
-  if (tid == 0) {
-    for (int s = 0; s < a.nstages; ++s) {
-      mbar_init(full0 + 8 * s, 1);
-      mbar_init(empty0 + 8 * s, 1);
-    }
-    fence_mbar_init();
+  const int64_t nw = static_cast<int64_t>(gridDim.x) * kWarps;
+  const int64_t wg = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
+  int64_t u0, u1, h0, h1;
+  split_range(I, nw, wg, u0, u1);   // phase 1: intermediate units
+  split_range(H, nw, wg, h0, h1);   // phase 2: down rows
+  const Walk<R> w1{a.gu_q, H, cdiv(u1 - u0, U), static_cast<int>(cdiv(H, kSegBytes)), 0};
+  const Walk<R> w2{a.down_q, I, cdiv(h1 - h0, R), static_cast<int>(cdiv(I, kSegBytes)),
+                   w1.items()};
+  auto row1 = [&](int64_t g, int r) -> int64_t {
+    const int64_t unit = u0 + g * U + (r % U);
+    if (unit >= u1) return -1;
+    return r < U ? unit : I + unit;
+  };
+  auto row2 = [&](int64_t g, int r) -> int64_t {
+    const int64_t row = h0 + g * R + r;
+    return row < h1 ? row : -1;
+  };
+  // ring position 0: the first phase-1 item, or phase 2's first if phase 1 is empty
+  Cursor c2 = cursor_at(w2, 0);   // next phase-2 item to issue
+  if (w1.ngrp > 0) {
+    issue_item<R, KM1>(w1, ring_s, cursor_at(w1, 0), lane, row1);
+  } else {
+    issue_item<R, KM2>(w2, ring_s, c2, lane, row2);
+    c2.next(w2.nseg);
   }
-  if (warp < kConsumerWarps) stage_x(xs, a.x, H, tid, kConsumerWarps * 32);
+  pdl_wait();
+  stage_x(xs, a.x, H, tid, kThreads);
   __syncthreads();
 
-  if (warp == kConsumerWarps) {
-    if (lane == 0) {
-      // Phase 1 then phase 2 positions in one sequence; each phase's copies
-      // use that phase's K (H, then I).
-      auto rows1 = [&](int pos) -> uint32_t {
-        const int64_t u0 = (ug_begin + pos / nseg1) * kUnits;
-        const int64_t units = min64(kUnits, I - u0);
-        const uint32_t m = (1u << units) - 1u;
-        return m | (m << kUnits);
-      };
-      auto src1 = [&](int pos, int r, int64_t k0) -> const void* {
-        const int64_t u0 = (ug_begin + pos / nseg1) * kUnits;
-        const int64_t row = r < kUnits ? u0 + r : I + u0 + (r - kUnits);
-        return a.gu_q + row * H + k0;
-      };
-      int issued = produce(full0, empty0, stage0, a.nstages, base2, nseg1, H, rows1, src1, 0x200u);
-      if (issued == base2) {
-        // Phase 2 continues the same ring: shift positions by base2.
-        auto rows2 = [&](int p) -> uint32_t {
-          const int64_t row0 = (rg_begin + p / nseg2) * kRW;
-          const int64_t rows = min64(kRW, H - row0);
-          return (1u << rows) - 1u;
-        };
-        auto src2 = [&](int p, int r, int64_t k0) -> const void* {
-          const int64_t row = (rg_begin + p / nseg2) * kRW + r;
-          return a.down_q + row * I + k0;
-        };
-        // produce() numbers positions from 0; run it on a shifted ring view.
-        const uint64_t pol = l2_evict_first_policy();
-        const int total2 = n2 * nseg2;
-        for (int p = 0; p < total2; ++p) {
-          const int pos = base2 + p;
-          const int s = pos % a.nstages;
-          const int use = pos / a.nstages;
-          if (use > 0 && !mbar_wait(empty0 + 8 * s, (use - 1) & 1)) {
-            report_error(ERR_WAIT_EMPTY, 0x203u);
-            break;
-          }
-          const int seg = p % nseg2;
-          const int64_t k0 = static_cast<int64_t>(seg) * kSeg;
-          const int sl = static_cast<int>(min64(kSeg, I - k0));
-          const uint32_t mask = rows2(p);
-          const uint32_t dst = stage0 + s * kStageBytes;
-          mbar_arrive_expect_tx(full0 + 8 * s, static_cast<uint32_t>(__popc(mask)) * sl);
-          if (nseg2 == 1) {
-            bulk_g2s(dst, src2(p, 0, 0), static_cast<uint32_t>(__popc(mask) * sl), full0 + 8 * s, pol);
-          } else {
-#pragma unroll 1
-            for (int r = 0; r < kRW; ++r)
-              if ((mask >> r) & 1u)
-                bulk_g2s(dst + r * sl, src2(p, r, k0), static_cast<uint32_t>(sl), full0 + 8 * s, pol);
-          }
-          ++issued;
-        }
+  // ---- phase 1 ----
+  auto scale1 = [&](int64_t g, int r, int64_t grp) -> float {
+    const int64_t row = row1(g, r);
+    return row >= 0 ? __ldg(a.gu_s + row * a.ng + grp) : 0.f;
+  };
+  auto done1 = [&](int64_t g, float s) {
+    // gate row r (< U) sits on lanes 4r..4r+3, its up row r + U on lane + 4U
+    const float up = __shfl_down_sync(0xffffffffu, s, 4 * U);
+    const int r = reduced_row<R>(lane);
+    if (r >= 0 && r < U) {
+      const int64_t unit = u0 + g * U + r;
+      if (unit < u1) {
+        const float ga = PER_ROW ? s * __ldg(a.gu_s + unit) : s;
+        const float ua = PER_ROW ? up * __ldg(a.gu_s + I + unit) : up;
+        a.abuf[unit] = ga / (1.0f + expf(-ga)) * ua;
       }
-      drain(full0, a.nstages, issued, 0x201u);
     }
+  };
+  auto into_phase2 = [&]() {
+    issue_item<R, KM2>(w2, ring_s, c2, lane, row2);
+    c2.next(w2.nseg);
+  };
+  walk<R, PER_ROW, KM1>(w1, ring_s, ring, reinterpret_cast<const uint8_t*>(xs), a.x, lane, H / a.ng,
+                        row1, scale1, into_phase2, done1);
+  pdl_trigger();
+
+  // ---- grid barrier, then phase 2 over abuf ----
+  const bool ok = grid_barrier(a.sync_ws, tid, 0x205u);
+  if (ok) stage_x<true>(xs, a.abuf, I, tid, kThreads);
+  __syncthreads();
+  if (!ok) {
+    cp_async_wait<0>();
     return;
   }
-
-  // ---- phase 1: gate/up GEMV pair + SiLU gate ----
-  bool ok = true;
-  for (int ugl = warp; ugl < n1; ugl += kConsumerWarps) {
-    const int64_t u0 = (ug_begin + ugl) * kUnits;
-    auto scale_of = [&](int r, int64_t g) -> float {
-      const int64_t unit = u0 + (r & (kUnits - 1));
-      if (unit >= I) return 0.f;
-      const int64_t row = r < kUnits ? unit : I + unit;
-      return __ldg(a.gu_s + row * a.ng + g);
-    };
-    float v[8];
-    if (!consume_group<PER_ROW>(full0, empty0, stage0, xs_base, a.nstages, ugl * nseg1, nseg1, H,
-                                G1, lane, scale_of, v, 0x204u)) {
-      ok = false;
-      break;
-    }
-    const float sum = warp_reduce8(v, lane);
-    const float up = __shfl_down_sync(0xffffffffu, sum, 16);
-    const int64_t unit = u0 + (lane >> 2);
-    if (lane < 16 && (lane & 3) == 0 && unit < I) {
-      const float ga = PER_ROW ? sum * __ldg(a.gu_s + unit) : sum;
-      const float ua = PER_ROW ? up * __ldg(a.gu_s + I + unit) : up;
-      a.abuf[unit] = ga / (1.0f + expf(-ga)) * ua;
-    }
-  }
-  // A warp that gave up still takes part in the CTA-level barriers below so
-  // the others are not left waiting; it just skips phase 2's work.
-  if (!grid_barrier(a.sync_ws, tid, 0x205u)) ok = false;
-  // ---- phase 2: down GEMV over abuf ----
-  stage_x<true>(xs, a.abuf, I, tid, kConsumerWarps * 32);
-  named_bar_sync(1, kConsumerWarps * 32);
-  if (!ok) return;
-  for (int rgl = warp; rgl < n2; rgl += kConsumerWarps) {
-    const int64_t row0 = (rg_begin + rgl) * kRW;
-    auto scale_of = [&](int r, int64_t g) -> float {
-      const int64_t row = row0 + r;
-      return row < H ? __ldg(a.down_s + row * a.ngd + g) : 0.f;
-    };
-    float v[8];
-    if (!consume_group<PER_ROW>(full0, empty0, stage0, xs_base, a.nstages, base2 + rgl * nseg2,
-                                nseg2, I, G2, lane, scale_of, v, 0x206u))
-      return;
-    const float sum = warp_reduce8(v, lane);
-    const int64_t row = row0 + ((lane >> 2) & 7);
-    if ((lane & 3) == 0 && row < H) {
-      float o = PER_ROW ? sum * __ldg(a.down_s + row) : sum;
+  auto scale2 = [&](int64_t g, int r, int64_t grp) -> float {
+    const int64_t row = row2(g, r);
+    return row >= 0 ? __ldg(a.down_s + row * a.ngd + grp) : 0.f;
+  };
+  auto done2 = [&](int64_t g, float s) {
+    const int r = reduced_row<R>(lane);
+    const int64_t row = h0 + g * R + r;
+    if (r >= 0 && row < h1) {
+      float o = PER_ROW ? s * __ldg(a.down_s + row) : s;
       if (a.residual) o += a.residual[row];
       a.out[row] = o;
     }
-  }
+  };
+  auto beyond = [&]() { cp_async_commit(); };
+  // phase 2 reads abuf from the staged copy (it was written by other CTAs)
+  walk<R, PER_ROW, KM2 == K1K ? KFULL : KM2>(w2, ring_s, ring,
+                                             reinterpret_cast<const uint8_t*>(xs), nullptr, lane,
+                                             I / a.ngd, row2, scale2, beyond, done2);
+  cp_async_wait<0>();
 }
 
 }  // namespace qz
