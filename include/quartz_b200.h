@@ -87,6 +87,33 @@ int qz_fused_mlp_decode(const int8_t* gu_q, const float* gu_s, int64_t ng, const
 int qz_mlp_workspace_bytes(void);
 
 /*
+ * qz_fused_mlp_decode without caller-provided scratch. No counterpart in the
+ * reference: the reference's fused_mlp_decode takes its abuf from the caller.
+ *
+ * For callers that cannot allocate device memory: a host engine or plugin
+ * whose device memory is owned by another allocator (a fixed pool or a
+ * framework's caching allocator) and that must not call cudaMalloc behind its
+ * back, or a caller with no allocation rights at all after start-up. This
+ * entry point allocates nothing (no cudaMalloc, cudaFree or allocating
+ * library call): the [I] intermediate and the grid-barrier words live in a
+ * file-scope __device__ array of 128.25 KB that every GPU loading the library
+ * holds until the process exits.
+ *
+ *   - I must be at most 32768; larger I returns QZ_ERR_INVALID.
+ *   - The first call on a device looks up the array's device address with
+ *     cudaGetSymbolAddress (with that device current). Make that first call
+ *     before any stream capture.
+ *   - All calls share the one array, which keeps the last call's intermediate.
+ *     The barrier count is cleared (cudaMemsetAsync on `stream`) at the start
+ *     of every call. Calls that overlap on the GPU (different streams, or
+ *     concurrent host threads) race on the array: serialise them.
+ * Arguments and results are those of qz_fused_mlp_decode minus abuf/sync_ws.
+ */
+int qz_fused_mlp_decode_noalloc(const int8_t* gu_q, const float* gu_s, int64_t ng, const float* x,
+                                const int8_t* down_q, const float* down_s, int64_t ngd, float* out,
+                                const float* residual, int64_t H, int64_t I, void* stream);
+
+/*
  * a[m, i] = silu(gu[m, i]) * gu[m, I + i], exponent clipped to [-88, 88].
  * The elementwise step of the M > 1 MLP (quartz/quantize.py:112-114 with
  * quartz/ops.py:35-37). gu is [M, 2I], a is [M, I].

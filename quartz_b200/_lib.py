@@ -30,6 +30,8 @@ SIGNATURES = {
     "qz_fused_mlp_decode": ([_vp, _vp, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _i64, _i64,
                              _vp, _vp], _int),
     "qz_mlp_workspace_bytes": ([], _int),
+    "qz_fused_mlp_decode_noalloc": ([_vp, _vp, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64,
+                                     _vp], _int),
     "qz_silu_mul": ([_vp, _vp, _i64, _i64, _vp], _int),
     "qz_device_status": ([ctypes.POINTER(ctypes.c_uint32), _int], _int),
     "qz_sync": ([_vp], _int),

@@ -307,6 +307,68 @@ int qz_fused_mlp_decode(const int8_t* gu_q, const float* gu_s, int64_t ng, const
   return tall ? launch_mlp_k<kTallRows, false>(*d, a, st) : launch_mlp_k<2, false>(*d, a, st);
 }
 
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free fused MLP. Its scratch (the [I] intermediate and the grid
+// barrier words) lives in this file-scope device array instead of buffers the
+// caller allocates. Every GPU that loads the library holds the array
+// (kNoAllocMaxI * 4 + 256 bytes = 128.25 KB) until the process exits.
+// ---------------------------------------------------------------------------
+namespace {
+constexpr int64_t kNoAllocMaxI = 32768;      // largest intermediate size accepted
+constexpr int64_t kNoAllocBarrierWords = 64; // qz_mlp_workspace_bytes() / 4
+}  // namespace
+
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocMaxI + kNoAllocBarrierWords];
+
+namespace {
+struct NoAllocScratch {
+  std::once_flag once;
+  float* ptr = nullptr;
+  cudaError_t err = cudaSuccess;
+};
+NoAllocScratch g_noalloc[kMaxDevices];
+
+// Device address of the scratch array on the current device, looked up once
+// per device (with that device current) on the first call there.
+int noalloc_scratch(float** out) {
+  int dev = 0;
+  QZ_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(QZ_ERR_UNSUPPORTED, "device index out of range");
+  NoAllocScratch& s = g_noalloc[dev];
+  std::call_once(s.once, [&] {
+    s.err = cudaGetSymbolAddress(reinterpret_cast<void**>(&s.ptr), g_noalloc_scratch);
+  });
+  if (s.err != cudaSuccess)
+    return fail(QZ_ERR_CUDA, std::string("cudaGetSymbolAddress(no-alloc scratch): ") +
+                                 cudaGetErrorString(s.err));
+  *out = s.ptr;
+  return QZ_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int qz_fused_mlp_decode_noalloc(const int8_t* gu_q, const float* gu_s, int64_t ng, const float* x,
+                                const int8_t* down_q, const float* down_s, int64_t ngd, float* out,
+                                const float* residual, int64_t H, int64_t I, void* stream) {
+  if (I < 0 || I > kNoAllocMaxI)
+    return fail(QZ_ERR_INVALID,
+                "qz_fused_mlp_decode_noalloc: I=" + std::to_string(I) +
+                    " is outside the built-in scratch capacity [0, " +
+                    std::to_string(kNoAllocMaxI) +
+                    "]; call qz_fused_mlp_decode with caller-owned abuf and sync_ws instead");
+  float* scratch = nullptr;
+  if (int rc = noalloc_scratch(&scratch)) return rc;
+  uint32_t* barrier = reinterpret_cast<uint32_t*>(scratch + kNoAllocMaxI);
+  // The barrier's arrival count must be zero when a call starts; a call whose
+  // wait gave up could have left it otherwise, so clear it (stream-ordered).
+  QZ_CUDA(cudaMemsetAsync(barrier, 0, sizeof(uint32_t), static_cast<cudaStream_t>(stream)));
+  return qz_fused_mlp_decode(gu_q, gu_s, ng, x, down_q, down_s, ngd, scratch, out, residual, H, I,
+                             barrier, stream);
+}
+
 int qz_silu_mul(const float* gu, float* a, int64_t M, int64_t I, void* stream) {
   if (M < 0 || I < 0) return fail(QZ_ERR_INVALID, "qz_silu_mul: negative dimension");
   if (M == 0 || I == 0) return QZ_OK;
