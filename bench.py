@@ -34,8 +34,9 @@ import numpy as np
 REPO = Path(__file__).resolve().parent
 sys.path.insert(0, str(REPO))
 
-from quartz_b200.workloads import (LM_HEAD_K, LM_HEAD_N, gemv_algorithmic_bytes,  # noqa: E402
-                                   gemv_case)
+from quartz_b200.workloads import (LM_HEAD_K, LM_HEAD_N, MLP_H, MLP_I, MLP_LAYER_SEED0,  # noqa: E402
+                                   MLP_LAYERS, gemv_algorithmic_bytes, gemv_case,
+                                   mlp_algorithmic_bytes, mlp_case)
 
 METRIC = "int8 GEMV achieved HBM GB/s (% of B200 peak); all-int8 decode tok/s"
 UNIT = "GB/s"
@@ -184,6 +185,84 @@ def run_reference(args) -> dict:
 # ---------------------------------------------------------------------------
 # GPU side
 # ---------------------------------------------------------------------------
+def run_mlp_body(args, dev) -> dict:
+    """Fused int8 MLP body at Qwen3-0.6B shape, M = 1: one step runs the 28
+    independently seeded layers (seed 1000 + l) back to back, each on its own
+    x, as one CUDA graph. 28 x 9.47 MB of weights per step (> L2)."""
+    import torch
+    from quartz_b200 import device as qdev
+    import oracle
+
+    layers = [mlp_case(MLP_H, MLP_I, seed=MLP_LAYER_SEED0 + l) for l in range(MLP_LAYERS)]
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev)  # noqa: E731
+    W = [(t(m.gu_q), t(m.gu_s), t(m.down_q), t(m.down_s)) for m in layers]
+    X = [t(m.x[0]) for m in layers]
+    A = [torch.empty(MLP_I, dtype=torch.float32, device=dev) for _ in layers]
+    O = [torch.empty(MLP_H, dtype=torch.float32, device=dev) for _ in layers]
+
+    def step():
+        for l in range(MLP_LAYERS):
+            gq, gs, dq, ds = W[l]
+            qdev.fused_mlp(gq, gs, X[l], dq, ds, A[l], O[l])
+
+    # parity gate: layer 0 and 27 against the oracle
+    step()
+    torch.cuda.synchronize()
+    for l in (0, MLP_LAYERS - 1):
+        m = layers[l]
+        ref = np.empty(MLP_H, np.float32)
+        oracle.fused_mlp_decode(m.gu_q, m.gu_s, m.x[0], m.down_q, m.down_s,
+                                np.empty(MLP_I, np.float32), ref)
+        rel = float(np.abs(O[l].cpu().numpy() - ref).max() / np.abs(ref).max())
+        if rel > 1e-4:
+            raise SystemExit(f"mlp parity failed on layer {l}: rel err {rel:.3e}")
+    stream = torch.cuda.current_stream()
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(stream)
+    with torch.cuda.stream(s):
+        step()
+    stream.wait_stream(s)
+    torch.cuda.synchronize()
+    with torch.cuda.graph(g):
+        step()
+    for _ in range(max(3, args.warmup // 10)):
+        g.replay()
+    torch.cuda.synchronize()
+    steps = max(10, args.steps // 20)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        g.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    qdev.check_status()
+    ms = e0.elapsed_time(e1) / steps
+    per_layer = mlp_algorithmic_bytes(MLP_H, MLP_I)
+    gbs = per_layer * MLP_LAYERS / (ms * 1e-3) / 1e9
+    out = {"workload": "qwen3-0.6b MLP body, 28 fused int8 MLP layers (H=1024, I=3072), M=1",
+           "value": round(gbs, 1), "unit": UNIT, "us_per_layer": round(ms * 1e3 / MLP_LAYERS, 3),
+           "steps": steps, "bytes_per_layer": per_layer, "gpu_launches": steps * MLP_LAYERS}
+    if not args.no_cpu:
+        oracle.set_threads(_cpu_cores())
+        abuf = np.empty(MLP_I, np.float32)
+        o = np.empty(MLP_H, np.float32)
+        ts = []
+        for _ in range(5):
+            t0 = time.perf_counter()
+            for m in layers:
+                oracle.fused_mlp_decode(m.gu_q, m.gu_s, m.x[0], m.down_q, m.down_s, abuf, o)
+            ts.append(time.perf_counter() - t0)
+        cm = statistics.median(ts)
+        out["cpu_baseline"] = {"value": round(per_layer * MLP_LAYERS / cm / 1e9, 2), "unit": UNIT,
+                               "cores": oracle.threads(), "kind": "port",
+                               "sample": f"28 layers, median of 5 passes "
+                                         f"({cm / MLP_LAYERS * 1e6:.1f} us per layer)"}
+    del g
+    return out
+
+
 def run_ours(args) -> dict:
     import torch
     from quartz_b200 import device as qdev
@@ -291,6 +370,8 @@ def run_ours(args) -> dict:
                "sample": f"full lm_head GEMV, median of {args.cpu_reps} calls "
                          f"({cmed * 1e3:.3f} ms each, {isa})"}
 
+    mlp = None if args.no_mlp else run_mlp_body(args, dev)
+
     traffic = None
     tpath = REPO / "profiles" / "gemv_lm_head_traffic.json"
     if tpath.exists():
@@ -312,6 +393,7 @@ def run_ours(args) -> dict:
         "cpu_baseline": cpu,
         "clocks": clk.summary(),
         "gpu_launches": args.steps,
+        "secondary": {"mlp_body": mlp},
     }
 
 
@@ -325,6 +407,7 @@ def main():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-mlp", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=500)
     ap.add_argument("--cpu-reps", type=int, default=30)
     args = ap.parse_args()

@@ -5,6 +5,7 @@
 
 #include <cstdio>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -135,9 +136,13 @@ int launch_generic_gemm(const DeviceInfo& d, const int8_t* q, const float* scale
   return QZ_OK;
 }
 
-// Launch `fn` with programmatic stream serialisation (and optionally as a
-// cooperative grid). Kernels launched this way issue their first weight
-// copies before griddepcontrol.wait, overlapping the previous kernel's tail.
+// Launch `fn` with programmatic stream serialisation (and, for the fused MLP,
+// as a cooperative grid too). Kernels launched this way issue their first
+// weight copies before griddepcontrol.wait, overlapping the previous kernel's
+// tail. If the runtime refuses cooperative + programmatic together, the
+// cooperative launch is retried alone and that choice is remembered.
+std::atomic<int> g_coop_pdl{1};
+
 template <class... Args>
 int launch_ex(void (*fn)(Args...), int grid, int smem, cudaStream_t st, bool cooperative,
               Args... args) {
@@ -146,17 +151,30 @@ int launch_ex(void (*fn)(Args...), int grid, int smem, cudaStream_t st, bool coo
   cfg.blockDim = dim3(qz::kThreads);
   cfg.dynamicSmemBytes = static_cast<size_t>(smem);
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  const bool pdl = !cooperative || g_coop_pdl.load(std::memory_order_relaxed);
+  if (pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
   if (cooperative) {
-    attr[0].id = cudaLaunchAttributeCooperative;
-    attr[0].val.cooperative = 1;
-  } else {
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[n].id = cudaLaunchAttributeCooperative;
+    attr[n].val.cooperative = 1;
+    ++n;
   }
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  QZ_CUDA(cudaLaunchKernelEx(&cfg, fn, args...));
+  cfg.numAttrs = n;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, fn, args...);
+  if (e != cudaSuccess && cooperative && pdl) {
+    (void)cudaGetLastError();
+    g_coop_pdl.store(0, std::memory_order_relaxed);
+    cfg.attrs = attr + 1;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, fn, args...);
+  }
+  QZ_CUDA(e);
   return QZ_OK;
 }
 

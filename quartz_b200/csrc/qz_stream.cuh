@@ -127,7 +127,7 @@ __device__ __forceinline__ void load_x16(const uint8_t* xs, int64_t nch, int64_t
 // (pos0 + item) % kDepth, so two walks can share one ring back to back.
 // Cursors advance item by item without divisions.
 // ---------------------------------------------------------------------------
-template <int R>
+template <int R, int D = kDepth>
 struct Walk {
   const int8_t* q;
   int64_t K;        // row length in bytes
@@ -137,29 +137,30 @@ struct Walk {
   __device__ int64_t items() const { return ngrp * nseg; }
 };
 
+template <int D>
 struct Cursor {
   int64_t g;        // row group
   int seg;          // K segment
   int slot;         // ring slot
   __device__ void next(int nseg) {
     if (++seg == nseg) { seg = 0; ++g; }
-    slot = slot + 1 == kDepth ? 0 : slot + 1;
+    slot = slot + 1 == D ? 0 : slot + 1;
   }
 };
 
-template <int R>
-__device__ __forceinline__ Cursor cursor_at(const Walk<R>& w, int64_t it) {
-  Cursor c;
+template <int R, int D>
+__device__ __forceinline__ Cursor<D> cursor_at(const Walk<R, D>& w, int64_t it) {
+  Cursor<D> c;
   c.g = it / w.nseg;
   c.seg = static_cast<int>(it - c.g * w.nseg);
-  c.slot = static_cast<int>((w.pos0 + it) % kDepth);
+  c.slot = static_cast<int>((w.pos0 + it) % D);
   return c;
 }
 
 // Issue the copies of the item at cursor c (if it exists), then commit one
 // cp.async group. rowfn(g, r) -> global row index, or -1 when absent.
-template <int R, int KM, class RowFn>
-__device__ __forceinline__ void issue_item(const Walk<R>& w, uint32_t ring, const Cursor& c,
+template <int R, int KM, int D, class RowFn>
+__device__ __forceinline__ void issue_item(const Walk<R, D>& w, uint32_t ring, const Cursor<D>& c,
                                            int lane, RowFn rowfn) {
   if (c.g < w.ngrp) {
     const int64_t k0 = KM == K1K ? 0 : static_cast<int64_t>(c.seg) * kSegBytes;
@@ -187,10 +188,10 @@ __device__ __forceinline__ void issue_item(const Walk<R>& w, uint32_t ring, cons
 // Otherwise each 16-element chunk's dot is weighted by its group's scale
 // scale_of(g, r, group) (G % 16 == 0, so a chunk never straddles groups).
 // K1K: xr holds this lane's 2 chunks of activations (loaded once per walk).
-template <int R, bool PER_ROW, int KM, class ScaleFn>
-__device__ __forceinline__ void accumulate_item(const Walk<R>& w, const uint8_t* ring,
+template <int R, bool PER_ROW, int KM, int D, class ScaleFn>
+__device__ __forceinline__ void accumulate_item(const Walk<R, D>& w, const uint8_t* ring,
                                                 const uint8_t* xs, const f2_t (&xr)[2][8],
-                                                const Cursor& c, int lane, int64_t G,
+                                                const Cursor<D>& c, int lane, int64_t G,
                                                 f2_t (&acc)[R], float (&accs)[R],
                                                 ScaleFn scale_of) {
   const int64_t k0 = KM == K1K ? 0 : static_cast<int64_t>(c.seg) * kSegBytes;
@@ -282,33 +283,40 @@ __device__ __forceinline__ void load_x_regs(const float* x, int lane, f2_t (&xr)
   }
 }
 
-// One walk through the ring. Before the call, the positions of items
-// 0 .. kDepth-2 have been issued (committed as one group each). Each step
-// issues the item kDepth-1 ahead (past the end: `beyond()` issues the next
-// walk's item or an empty group), waits for the current item and accumulates
-// it; at a group's last segment `done(g, sum)` runs on every lane (sum is
-// meaningful on the lanes reduced_row<R>() names).
-// K1K walks take their activations from `xg` (global) into registers;
-// the others read the CTA's staged copy `xs` item by item.
-template <int R, bool PER_ROW, int KM, class RowFn, class ScaleFn, class BeyondFn, class DoneFn>
-__device__ __forceinline__ void walk(const Walk<R>& w, uint32_t ring_s, const uint8_t* ring,
+// Issue items [from, to) of a walk, one cp.async group each.
+template <int R, int KM, int D, class RowFn>
+__device__ __forceinline__ void issue_items(const Walk<R, D>& w, uint32_t ring, int64_t from,
+                                            int64_t to, int lane, RowFn rowfn) {
+  Cursor<D> c = cursor_at(w, from);
+  for (int64_t it = from; it < to; ++it, c.next(w.nseg)) issue_item<R, KM>(w, ring, c, lane, rowfn);
+}
+
+// One walk through a ring of D slots. Before the call, the positions of items
+// 0 .. D-2 have been issued (committed as one group each, empty groups for
+// missing items). Each step issues the item D-1 ahead (past the end:
+// `beyond()` issues the next walk's item or an empty group), waits for the
+// current item and accumulates it; at a group's last segment `done(g, sum)`
+// runs on every lane (sum is meaningful on the lanes reduced_row<R>() names).
+// K1K walks take their activations from `xg` (global) into registers; the
+// others read the CTA's staged copy `xs` item by item.
+template <int R, bool PER_ROW, int KM, int D, class RowFn, class ScaleFn, class BeyondFn,
+          class DoneFn>
+__device__ __forceinline__ void walk(const Walk<R, D>& w, uint32_t ring_s, const uint8_t* ring,
                                      const uint8_t* xs, const float* xg, int lane, int64_t G,
                                      RowFn rowfn, ScaleFn scale_of, BeyondFn beyond,
                                      DoneFn done) {
-  static_assert(kDepth == 2, "the look-ahead cursor below assumes a two-slot ring");
   f2_t xr[2][8];
   if constexpr (KM == K1K) load_x_regs(xg, lane, xr);
   f2_t acc[R];
   float accs[R];
-  Cursor cur = cursor_at(w, 0);
-  Cursor ahead = cur;
-  ahead.next(w.nseg);
+  Cursor<D> cur = cursor_at(w, 0);
+  Cursor<D> ahead = cursor_at(w, D - 1);
   for (; cur.g < w.ngrp; cur.next(w.nseg), ahead.next(w.nseg)) {
     if (ahead.g < w.ngrp)
       issue_item<R, KM>(w, ring_s, ahead, lane, rowfn);
     else
       beyond();
-    cp_async_wait<kDepth - 1>();
+    cp_async_wait<D - 1>();
     if (cur.seg == 0) {
 #pragma unroll
       for (int r = 0; r < R; ++r) { acc[r] = 0ull; accs[r] = 0.f; }
@@ -412,9 +420,13 @@ __device__ __forceinline__ bool grid_barrier(unsigned int* ws, int tid, unsigned
 
 template <int R, bool PER_ROW, int KM1, int KM2, int MINB>
 __global__ void __launch_bounds__(kThreads, MINB) fused_mlp_kernel(const MlpArgs a) {
-  static_assert(kDepth == 2, "phase hand-over below assumes a two-slot ring");
   static_assert(R % 2 == 0, "a unit group holds R/2 gate rows and R/2 up rows");
   constexpr int U = R / 2;
+  // Phase 2 walks one down row per group through the same per-warp ring,
+  // re-cut into D2 slots of 1 KB; up to D2 - 1 of its items are issued before
+  // the grid barrier, so for small layers all of phase 2's weights are in
+  // shared memory by the time abuf is ready.
+  constexpr int D2 = kDepth * R;
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t H = a.H, I = a.I;
@@ -428,25 +440,15 @@ __global__ void __launch_bounds__(kThreads, MINB) fused_mlp_kernel(const MlpArgs
   split_range(I, nw, wg, u0, u1);   // phase 1: intermediate units
   split_range(H, nw, wg, h0, h1);   // phase 2: down rows
   const Walk<R> w1{a.gu_q, H, cdiv(u1 - u0, U), static_cast<int>(cdiv(H, kSegBytes)), 0};
-  const Walk<R> w2{a.down_q, I, cdiv(h1 - h0, R), static_cast<int>(cdiv(I, kSegBytes)),
-                   w1.items()};
+  const Walk<1, D2> w2{a.down_q, I, h1 - h0, static_cast<int>(cdiv(I, kSegBytes)), 0};
   auto row1 = [&](int64_t g, int r) -> int64_t {
     const int64_t unit = u0 + g * U + (r % U);
     if (unit >= u1) return -1;
     return r < U ? unit : I + unit;
   };
-  auto row2 = [&](int64_t g, int r) -> int64_t {
-    const int64_t row = h0 + g * R + r;
-    return row < h1 ? row : -1;
-  };
-  // ring position 0: the first phase-1 item, or phase 2's first if phase 1 is empty
-  Cursor c2 = cursor_at(w2, 0);   // next phase-2 item to issue
-  if (w1.ngrp > 0) {
-    issue_item<R, KM1>(w1, ring_s, cursor_at(w1, 0), lane, row1);
-  } else {
-    issue_item<R, KM2>(w2, ring_s, c2, lane, row2);
-    c2.next(w2.nseg);
-  }
+  auto row2 = [&](int64_t g, int) -> int64_t { return h0 + g < h1 ? h0 + g : -1; };
+
+  issue_item<R, KM1>(w1, ring_s, cursor_at(w1, 0), lane, row1);
   pdl_wait();
   stage_x(xs, a.x, H, tid, kThreads);
   __syncthreads();
@@ -469,12 +471,13 @@ __global__ void __launch_bounds__(kThreads, MINB) fused_mlp_kernel(const MlpArgs
       }
     }
   };
-  auto into_phase2 = [&]() {
-    issue_item<R, KM2>(w2, ring_s, c2, lane, row2);
-    c2.next(w2.nseg);
-  };
-  walk<R, PER_ROW, KM1>(w1, ring_s, ring, reinterpret_cast<const uint8_t*>(xs), a.x, lane, H / a.ng,
-                        row1, scale1, into_phase2, done1);
+  auto empty_group = [&]() { cp_async_commit(); };
+  walk<R, PER_ROW, KM1>(w1, ring_s, ring, reinterpret_cast<const uint8_t*>(xs), a.x, lane,
+                        H / a.ng, row1, scale1, empty_group, done1);
+  // The ring is free again (phase 1 consumed every item): prefetch phase 2.
+  cp_async_wait<0>();
+  __syncwarp();
+  issue_items<1, KM2>(w2, ring_s, 0, D2 - 1, lane, row2);
   pdl_trigger();
 
   // ---- grid barrier, then phase 2 over abuf ----
@@ -485,24 +488,21 @@ __global__ void __launch_bounds__(kThreads, MINB) fused_mlp_kernel(const MlpArgs
     cp_async_wait<0>();
     return;
   }
-  auto scale2 = [&](int64_t g, int r, int64_t grp) -> float {
-    const int64_t row = row2(g, r);
-    return row >= 0 ? __ldg(a.down_s + row * a.ngd + grp) : 0.f;
+  auto scale2 = [&](int64_t g, int, int64_t grp) -> float {
+    return h0 + g < h1 ? __ldg(a.down_s + (h0 + g) * a.ngd + grp) : 0.f;
   };
   auto done2 = [&](int64_t g, float s) {
-    const int r = reduced_row<R>(lane);
-    const int64_t row = h0 + g * R + r;
-    if (r >= 0 && row < h1) {
+    const int64_t row = h0 + g;
+    if (lane == 0 && row < h1) {
       float o = PER_ROW ? s * __ldg(a.down_s + row) : s;
       if (a.residual) o += a.residual[row];
       a.out[row] = o;
     }
   };
-  auto beyond = [&]() { cp_async_commit(); };
   // phase 2 reads abuf from the staged copy (it was written by other CTAs)
-  walk<R, PER_ROW, KM2 == K1K ? KFULL : KM2>(w2, ring_s, ring,
+  walk<1, PER_ROW, KM2 == K1K ? KFULL : KM2>(w2, ring_s, ring,
                                              reinterpret_cast<const uint8_t*>(xs), nullptr, lane,
-                                             I / a.ngd, row2, scale2, beyond, done2);
+                                             I / a.ngd, row2, scale2, empty_group, done2);
   cp_async_wait<0>();
 }
 
