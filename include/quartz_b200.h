@@ -68,6 +68,29 @@ int qz_gemm_w8(const int8_t* q, const float* scale, int64_t ng, const float* X, 
                int64_t M, int64_t N, int64_t K, const float* residual, void* stream);
 
 /*
+ * Bytes of device workspace qz_gemm_w8_ws can use for an [M, K] x [N, K]^T
+ * product (0 when M < 2), written to *bytes: the activation limbs and row
+ * scales, plus int32 partial sums for splitting K across CTAs when the output
+ * has too few 128-row tiles to fill the GPU.
+ */
+int qz_gemm_w8_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t* bytes);
+
+/*
+ * qz_gemm_w8 on the tensor cores. With ng == 1, K % 16 == 0, q 16-byte
+ * aligned and a 16-byte aligned workspace of qz_gemm_w8_workspace_bytes(M, N, K)
+ * bytes, M > 1 runs the tcgen05 kernel: X is split into three int8 limbs with
+ * a per-row scale (a 24-bit fixed-point copy, error <= max|X[m,:]| * 2^-24 per
+ * element) and every limb is multiplied by the int8 weights with exact int32
+ * accumulation in tensor memory (split-K partials add exactly, so results do
+ * not depend on the split). Otherwise it behaves as qz_gemm_w8. Calls sharing
+ * one workspace must not overlap on the GPU.
+ * Replaces w8a32_gemm (quartz/kernels/int8.py:66-87) for batched rows.
+ */
+int qz_gemm_w8_ws(const int8_t* q, const float* scale, int64_t ng, const float* X, float* Y,
+                  int64_t M, int64_t N, int64_t K, const float* residual, void* workspace,
+                  size_t workspace_bytes, void* stream);
+
+/*
  * out[h] = sum down[h, :] * abuf * down_s  (+ residual[h]),
  *   abuf[n] = silu(gate_n . x) * (up_n . x)     (silu with unclipped exp)
  * Replaces fused_mlp_decode (quartz/kernels/fused.py:27-65).

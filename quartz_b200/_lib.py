@@ -29,6 +29,9 @@ SIGNATURES = {
     "qz_gemm_w8": ([_vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _vp, _vp], _int),
     "qz_fused_mlp_decode": ([_vp, _vp, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _i64, _i64,
                              _vp, _vp], _int),
+    "qz_gemm_w8_workspace_bytes": ([_i64, _i64, _i64, ctypes.POINTER(_i64)], _int),
+    "qz_gemm_w8_ws": ([_vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _vp, _vp, ctypes.c_size_t, _vp],
+                      _int),
     "qz_mlp_workspace_bytes": ([], _int),
     "qz_fused_mlp_decode_noalloc": ([_vp, _vp, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64,
                                      _vp], _int),

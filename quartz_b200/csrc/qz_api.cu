@@ -12,6 +12,7 @@
 #include "quartz_b200.h"
 #include "qz_generic.cuh"
 #include "qz_stream.cuh"
+#include "qz_tc_gemm.cuh"
 
 namespace {
 
@@ -245,6 +246,145 @@ int launch_mlp_k(const DeviceInfo& d, const qz::MlpArgs& a, cudaStream_t st) {
   return launch_mlp<R, PER_ROW, qz::KANY>(d, a, st);
 }
 
+// ---------------------------------------------------------------------------
+// tcgen05 GEMM (M > 1): TMA descriptors, workspace layout, launch
+// ---------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                  const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                  const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                  CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+int encode_tiled_fn(EncodeTiledFn* out) {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  static cudaError_t err = cudaSuccess;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    err = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    if (err == cudaSuccess && q != cudaDriverEntryPointSuccess) err = cudaErrorNotSupported;
+    fn = reinterpret_cast<EncodeTiledFn>(p);
+  });
+  if (err != cudaSuccess || !fn)
+    return fail(QZ_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled is not available");
+  *out = fn;
+  return QZ_OK;
+}
+
+// 2-D uint8 tensor [rows, cols] (row-major), tiles of box_rows x 128 bytes,
+// 128-byte swizzle.
+int make_tmap_u8(CUtensorMap* map, const void* base, int64_t rows, int64_t cols, int box_rows) {
+  EncodeTiledFn enc = nullptr;
+  if (int rc = encode_tiled_fn(&enc)) return rc;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(cols), static_cast<cuuint64_t>(rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(cols)};
+  const cuuint32_t box[2] = {static_cast<cuuint32_t>(qz::tc::kKBytes),
+                             static_cast<cuuint32_t>(box_rows)};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims,
+                         strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(QZ_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string(r));
+  return QZ_OK;
+}
+
+int tc_token_tile(int64_t M) {
+  const int64_t m16 = qz::cdiv(M, 16) * 16;
+  return m16 >= 128 ? 128 : m16 > 32 ? 64 : static_cast<int>(m16);
+}
+
+// Workspace: [3][Mpad][K] int8 limbs | Mpad fp32 row scales | (split-K)
+// [3][Mpad][N] int32 partial sums; each part 256-byte aligned.
+struct TcLayout {
+  int mt;
+  int64_t mpad, limb_bytes, sx_bytes, acc_bytes;
+  int64_t total() const { return limb_bytes + sx_bytes + acc_bytes; }
+};
+
+TcLayout tc_layout(int64_t M, int64_t N, int64_t K) {
+  TcLayout l;
+  l.mt = tc_token_tile(M);
+  l.mpad = qz::cdiv(M, l.mt) * l.mt;
+  auto al = [](int64_t b) { return ((b + 255) / 256) * 256; };
+  l.limb_bytes = al(qz::tc::kLimbs * l.mpad * K);
+  l.sx_bytes = al(l.mpad * 4);
+  l.acc_bytes = al(qz::tc::kLimbs * l.mpad * N * 4);
+  return l;
+}
+
+template <int MT>
+int launch_tc(const DeviceInfo& d, const CUtensorMap& tq, const CUtensorMap& tx,
+              const qz::tc::TcArgs& a0, int32_t* acc, cudaStream_t st) {
+  auto fn = qz::tc::gemm_i8_kernel<MT>;
+  constexpr int sb = qz::tc::stage_bytes(MT);
+  // dynamic = stages * sb + 1024 (alignment slack) + 512 (barriers, TMEM slot).
+  // Small token tiles: size the ring so two CTAs share an SM (one streams
+  // while the other runs its prologue/epilogue); large tiles: one CTA, deep ring.
+  const int per_cta = MT <= 32 ? d.smem_optin / 2 - 1024 : d.smem_optin - 256;
+  const int budget = per_cta - 1024 - 512;
+  const int64_t nk = qz::cdiv(a0.K, qz::tc::kKBytes);
+  const int stages = static_cast<int>(std::min<int64_t>(
+      std::min(qz::tc::kMaxStages, budget / sb), std::max<int64_t>(2, nk)));
+  if (stages < 2) return fail(QZ_ERR_UNSUPPORTED, "tc gemm: shared memory does not fit");
+  const int smem = stages * sb + 1024 + 512;
+  static std::once_flag once[kMaxDevices];
+  int dev = 0;
+  QZ_CUDA(cudaGetDevice(&dev));
+  cudaError_t ae = cudaSuccess;
+  std::call_once(once[dev], [&] { ae = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, d.smem_optin - 256); });
+  QZ_CUDA(ae);
+  qz::tc::TcArgs a = a0;
+  a.nstages = stages;
+  // Split K when the output tiles alone would leave SMs idle; the splits add
+  // exact int32 partial sums, so the result does not depend on their order.
+  const int64_t tiles = qz::cdiv(a.N, qz::tc::kRows) * (a.Mpad / MT);
+  const int64_t target = int64_t(d.sms) * (MT <= 32 ? 2 : 1);
+  a.splits = tiles >= d.sms || !acc ? 1
+                                    : static_cast<int>(std::min<int64_t>(nk, qz::cdiv(target, tiles)));
+  a.acc = a.splits > 1 ? acc : nullptr;
+  if (a.acc)
+    QZ_CUDA(cudaMemsetAsync(a.acc, 0, sizeof(int32_t) * qz::tc::kLimbs * a.Mpad * a.N, st));
+  const dim3 grid(static_cast<unsigned>(qz::cdiv(a.N, qz::tc::kRows)),
+                  static_cast<unsigned>(a.Mpad / MT), static_cast<unsigned>(a.splits));
+  fn<<<grid, qz::tc::kThreads, smem, st>>>(tq, tx, a);
+  QZ_CUDA(cudaGetLastError());
+  if (a.acc) {
+    const int64_t total = a.M * a.N;
+    const int blocks = static_cast<int>(std::min<int64_t>(qz::cdiv(total, 256), d.sms * 8));
+    qz::tc::splitk_finish_kernel<<<blocks, 256, 0, st>>>(a.acc, a.scale, a.sx, a.residual, a.Y,
+                                                        a.M, a.N, a.Mpad);
+    QZ_CUDA(cudaGetLastError());
+  }
+  return QZ_OK;
+}
+
+int tc_gemm(const DeviceInfo& d, const int8_t* q, const float* scale, const float* X, float* Y,
+            int64_t M, int64_t N, int64_t K, const float* residual, void* ws, size_t ws_bytes,
+            cudaStream_t st) {
+  const TcLayout L = tc_layout(M, N, K);
+  int8_t* limbs = static_cast<int8_t*>(ws);
+  float* sx = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + L.limb_bytes);
+  int32_t* acc = static_cast<int64_t>(ws_bytes) >= L.total()
+                     ? reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + L.limb_bytes +
+                                                  L.sx_bytes)
+                     : nullptr;
+  qz::tc::split_x_kernel<<<static_cast<unsigned>(L.mpad), 256, 0, st>>>(X, limbs, sx, M, L.mpad,
+                                                                          K);
+  QZ_CUDA(cudaGetLastError());
+  CUtensorMap tq, tx;
+  if (int rc = make_tmap_u8(&tq, q, N, K, qz::tc::kRows)) return rc;
+  if (int rc = make_tmap_u8(&tx, limbs, qz::tc::kLimbs * L.mpad, K, L.mt)) return rc;
+  const qz::tc::TcArgs a{scale, sx, Y, residual, nullptr, M, N, K, L.mpad, 0, 1};
+  switch (L.mt) {
+    case 16: return launch_tc<16>(d, tq, tx, a, acc, st);
+    case 32: return launch_tc<32>(d, tq, tx, a, acc, st);
+    case 64: return launch_tc<64>(d, tq, tx, a, acc, st);
+    default: return launch_tc<128>(d, tq, tx, a, acc, st);
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -285,6 +425,35 @@ int qz_gemm_w8(const int8_t* q, const float* scale, int64_t ng, const float* X, 
   DeviceInfo* d = nullptr;
   if (int rc = device_info(&d)) return rc;
   return launch_generic_gemm(*d, q, scale, ng, X, Y, residual, M, N, K, st);
+}
+
+int qz_gemm_w8_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t* bytes) {
+  if (!bytes) return fail(QZ_ERR_INVALID, "qz_gemm_w8_workspace_bytes: null bytes");
+  if (M < 0 || N < 0 || K < 0)
+    return fail(QZ_ERR_INVALID, "qz_gemm_w8_workspace_bytes: negative size");
+  *bytes = M >= 2 ? tc_layout(M, N, K).total() : 0;
+  return QZ_OK;
+}
+
+int qz_gemm_w8_ws(const int8_t* q, const float* scale, int64_t ng, const float* X, float* Y,
+                  int64_t M, int64_t N, int64_t K, const float* residual, void* workspace,
+                  size_t workspace_bytes, void* stream) {
+  if (int rc = check_weights(q, scale, ng, N, K, "qz_gemm_w8_ws")) return rc;
+  if (M < 0) return fail(QZ_ERR_INVALID, "qz_gemm_w8_ws: negative M");
+  if (M == 0 || N == 0) return QZ_OK;
+  if (!Y || (K > 0 && !X)) return fail(QZ_ERR_INVALID, "qz_gemm_w8_ws: null X or Y");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (M == 1) return gemv_impl(q, scale, ng, X, Y, N, K, residual, st);
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  // The tensor path needs at least the limb + row-scale part of the workspace;
+  // with the whole of it, it may also split K.
+  const TcLayout L = tc_layout(M, N, K);
+  const bool tensor = ng == 1 && K > 0 && K % 16 == 0 && aligned16(q) && workspace &&
+                      aligned16(workspace) &&
+                      static_cast<int64_t>(workspace_bytes) >= L.limb_bytes + L.sx_bytes;
+  if (!tensor) return launch_generic_gemm(*d, q, scale, ng, X, Y, residual, M, N, K, st);
+  return tc_gemm(*d, q, scale, X, Y, M, N, K, residual, workspace, workspace_bytes, st);
 }
 
 int qz_mlp_workspace_bytes(void) { return 256; }

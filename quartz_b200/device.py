@@ -22,6 +22,7 @@ from . import _lib
 _init_lock = threading.Lock()
 _ready_devices: set[int] = set()
 _mlp_ws: dict[int, torch.Tensor] = {}
+_gemm_ws: dict[int, torch.Tensor] = {}
 
 
 def _stream_ptr(dev: torch.device) -> int:
@@ -124,11 +125,33 @@ def gemm(q, scale, X, Y=None, residual=None):
         if residual.numel() != M * N:
             raise ValueError("residual must have M*N elements")
     _same_device(q.device, scale, X, Y, residual)
+    ws = gemm_workspace(q.device, M, N, K)
     with torch.cuda.device(q.device):
-        _lib.check(_lib.load().qz_gemm_w8(q.data_ptr(), scale.data_ptr(), ng, X.data_ptr(),
-                                          Y.data_ptr(), M, N, K, _ptr(residual),
-                                          _stream_ptr(q.device)))
+        _lib.check(_lib.load().qz_gemm_w8_ws(q.data_ptr(), scale.data_ptr(), ng, X.data_ptr(),
+                                             Y.data_ptr(), M, N, K, _ptr(residual),
+                                             _ptr(ws), 0 if ws is None else ws.numel(),
+                                             _stream_ptr(q.device)))
     return Y
+
+
+def gemm_workspace(device, M: int, N: int, K: int):
+    """Grow-only per-device workspace for the tensor-core GEMM (None when M < 2).
+
+    The GEMM's activation split is stream-ordered on the current stream; two
+    streams must not share this buffer concurrently.
+    """
+    import ctypes
+    idx = ensure_device(device)
+    need = ctypes.c_int64(0)
+    _lib.check(_lib.load().qz_gemm_w8_workspace_bytes(M, N, K, ctypes.byref(need)))
+    if need.value == 0:
+        return None
+    ws = _gemm_ws.get(idx)
+    if ws is None or ws.numel() < need.value:
+        ws = torch.empty(max(need.value, 1 << 20), dtype=torch.uint8,
+                         device=torch.device("cuda", idx))
+        _gemm_ws[idx] = ws
+    return ws
 
 
 def mlp_workspace(device) -> torch.Tensor:
