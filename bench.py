@@ -185,7 +185,7 @@ def run_reference(args) -> dict:
 # ---------------------------------------------------------------------------
 # GPU side
 # ---------------------------------------------------------------------------
-def run_mlp_body(args, dev) -> dict:
+def run_mlp_body(args, dev, world: int = 1, do_cpu: bool = True) -> dict:
     """Fused int8 MLP body at Qwen3-0.6B shape, M = 1: one step runs the 28
     independently seeded layers (seed 1000 + l) back to back, each on its own
     x, as one CUDA graph. 28 x 9.47 MB of weights per step (> L2)."""
@@ -232,19 +232,20 @@ def run_mlp_body(args, dev) -> dict:
     steps = max(10, args.steps // 20)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+    _barrier(world)
     e0.record(stream)
     for _ in range(steps):
         g.replay()
     e1.record(stream)
-    torch.cuda.synchronize()
-    qdev.check_status()
-    ms = e0.elapsed_time(e1) / steps
+    _barrier(world)
+    qdev.check_status(dev)
+    ms = _dist_max(e0.elapsed_time(e1) / steps, world)
     per_layer = mlp_algorithmic_bytes(MLP_H, MLP_I)
-    gbs = per_layer * MLP_LAYERS / (ms * 1e-3) / 1e9
+    gbs = world * per_layer * MLP_LAYERS / (ms * 1e-3) / 1e9
     out = {"workload": "qwen3-0.6b MLP body, 28 fused int8 MLP layers (H=1024, I=3072), M=1",
            "value": round(gbs, 1), "unit": UNIT, "us_per_layer": round(ms * 1e3 / MLP_LAYERS, 3),
            "steps": steps, "bytes_per_layer": per_layer, "gpu_launches": steps * MLP_LAYERS}
-    if not args.no_cpu:
+    if do_cpu:
         oracle.set_threads(_cpu_cores())
         abuf = np.empty(MLP_I, np.float32)
         o = np.empty(MLP_H, np.float32)
@@ -263,13 +264,92 @@ def run_mlp_body(args, dev) -> dict:
     return out
 
 
-def run_ours(args) -> dict:
+def _log(rank: int, msg: str) -> None:
+    if rank == 0:
+        print(f"[bench] {msg}", file=sys.stderr, flush=True)
+
+
+def _dist_max(value: float, world: int) -> float:
+    """Max of a per-rank float over all ranks (identity on one rank)."""
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device=torch.device("cuda", torch.cuda.current_device()))
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world: int) -> None:
+    import torch
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier(device_ids=[torch.cuda.current_device()])
+    torch.cuda.synchronize()
+
+
+def run_tp(args, rank: int, world: int, dev) -> dict:
+    """Tensor-parallel Qwen3-8B shapes (hidden 4096, MLP 12288, vocab 151936,
+    36 layers): per step, the 36 MLP layers (gate/up column-parallel, down
+    row-parallel, all-reduce of the partials) and the vocab-parallel lm_head
+    with the greedy (max, index) all-gather. Strong scaling: the whole model's
+    int8 weights are split over the ranks. Weights are drawn on the device
+    (int8 uniform, fp32 scales): timing does not depend on their values;
+    parity of this path is covered by the tests."""
+    import torch
+    from quartz_b200.sharding import ShardedLMHead, ShardedMLP, shard_range
+    H, I, V, L = 4096, 12288, 151936, 36
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1234 + rank)
+
+    def q_(shape):
+        return torch.randint(-127, 128, shape, dtype=torch.int8, device=dev, generator=gen)
+
+    def s_(n):
+        return torch.rand((n, 1), device=dev, generator=gen) * 2e-4 + 1e-4
+
+    lo, hi = shard_range(V, world, rank)
+    head = ShardedLMHead.from_local(q_((hi - lo, H)), s_(hi - lo), V)
+    ulo, uhi = shard_range(I, world, rank)
+    layers = [ShardedMLP.from_local(q_((2 * (uhi - ulo), H)), s_(2 * (uhi - ulo)),
+                                    q_((H, uhi - ulo)), s_(H), I) for _ in range(L)]
+    weight_bytes = V * H + L * 3 * I * H
+    out = {"workload": "qwen3-8b shapes: 36 TP MLP layers + vocab-parallel lm_head argmax",
+           "n_gpus": world, "scaling": "strong", "weight_bytes": weight_bytes}
+    for M in (1, 16):
+        x = torch.randn((M, H), device=dev, generator=gen)
+
+        def step():
+            for mlp in layers:
+                mlp(x)
+            return head.argmax(x)
+
+        for _ in range(3):
+            step()
+        _barrier(world)
+        steps = 10
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(steps):
+            step()
+        t1.record()
+        _barrier(world)
+        ms = _dist_max(t0.elapsed_time(t1) / steps, world)
+        out[f"M{M}"] = {"ms_per_step": round(ms, 4), "tok_per_s": round(M / (ms * 1e-3), 1),
+                        "weight_GBs": round(weight_bytes / (ms * 1e-3) / 1e9, 1)}
+    del layers, head
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     import torch
     from quartz_b200 import device as qdev
     from quartz_b200 import kernels as qk
 
-    torch.cuda.set_device(0)
-    dev = torch.device("cuda:0")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
     qdev.ensure_device(dev)
     qdev.status(clear=True)
 
@@ -294,7 +374,7 @@ def run_ours(args) -> dict:
     torch.cuda.synchronize()
     rel = float(np.abs(ys[0].cpu().numpy() - y_ref).max() / np.abs(y_ref).max())
     if rel > 1e-4:
-        raise SystemExit(f"parity check failed before timing: rel err {rel:.3e}")
+        raise SystemExit(f"parity check failed before timing on rank {rank}: rel err {rel:.3e}")
 
     stream = torch.cuda.current_stream()
     use_graph = not args.no_graph
@@ -325,18 +405,21 @@ def run_ours(args) -> dict:
                 step(i)
 
     run(args.warmup)
-    torch.cuda.synchronize()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
-    with ClockSampler(torch.cuda.current_device()) as clk:
-        torch.cuda.synchronize()
-        start.record(stream)
-        run(args.steps)
-        end.record(stream)
-        torch.cuda.synchronize()
-    ms = start.elapsed_time(end) / args.steps
-    qdev.check_status()
-    gbs = nbytes / (ms * 1e-3) / 1e9
+    clk = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    if clk:
+        clk.__enter__()
+    _barrier(world)
+    start.record(stream)
+    run(args.steps)
+    end.record(stream)
+    _barrier(world)
+    if clk:
+        clk.__exit__(None, None, None)
+    ms = _dist_max(start.elapsed_time(end) / args.steps, world)
+    qdev.check_status(dev)
+    gbs = world * nbytes / (ms * 1e-3) / 1e9
     peak, peak_kind = _peaks()
 
     # e2e: public numpy API, host x in and host y out every step
@@ -351,49 +434,62 @@ def run_ours(args) -> dict:
         for i in range(args.warmup):
             qk.w8a32_gemv(qnp[i % copies], snp[i % copies], xh, yh)
         esteps = max(1, min(args.steps, args.e2e_steps))
+        _barrier(world)
         t0 = time.perf_counter()
         for i in range(esteps):
             qk.w8a32_gemv(qnp[i % copies], snp[i % copies], xh, yh)
-        et = (time.perf_counter() - t0) / esteps
+        et = _dist_max((time.perf_counter() - t0) / esteps, world)
         rel_e = float(np.abs(yh - y_ref).max() / np.abs(y_ref).max())
         if rel_e > 1e-4:
             raise SystemExit(f"e2e parity failed: rel err {rel_e:.3e}")
-        e2e = {"value": round(nbytes / et / 1e9, 2), "unit": UNIT,
+        e2e = {"value": round(world * nbytes / et / 1e9, 2), "unit": UNIT,
                "h2d_bytes_per_step": int(xh.nbytes), "d2h_bytes_per_step": int(yh.nbytes),
                "ms_per_step": round(et * 1e3, 4), "steps": esteps,
-               "note": "numpy w8a32_gemv; int8 weights resident after first use"}
+               "note": "numpy w8a32_gemv per rank; int8 weights resident after first use"}
 
     cpu = None
-    if not args.no_cpu:
+    if not args.no_cpu and world == 1:
         cgbs, cmed, cthreads, isa = cpu_gemv_gbs(case, reps=args.cpu_reps, threads=_cpu_cores())
         cpu = {"value": round(cgbs, 3), "unit": UNIT, "cores": cthreads, "kind": "port",
                "sample": f"full lm_head GEMV, median of {args.cpu_reps} calls "
                          f"({cmed * 1e3:.3f} ms each, {isa})"}
 
-    mlp = None if args.no_mlp else run_mlp_body(args, dev)
+    _log(rank, f"lm_head GEMV {ms * 1e3:.2f} us/step; e2e and cpu done")
+    mlp = None
+    if not args.no_mlp:
+        mlp = run_mlp_body(args, dev, world=world, do_cpu=(world == 1 and not args.no_cpu))
+    _log(rank, "mlp body done")
+    tp = None if args.no_tp else run_tp(args, rank, world, dev)
+    _log(rank, "tensor-parallel block done")
+    if use_graph:
+        del g
 
+    if rank != 0:
+        return None
     traffic = None
     tpath = REPO / "profiles" / "gemv_lm_head_traffic.json"
     if tpath.exists():
         traffic = json.loads(tpath.read_text()).get("dram_bytes_per_launch")
     achieved = nbytes / (ms * 1e-3) / 1e9
     return {
-        "metric": METRIC, "value": round(gbs, 2), "unit": UNIT, "n_gpus": 1,
+        "metric": METRIC, "value": round(gbs, 2), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int8 weights, fp32 accumulate", "data": "synthetic",
         "config": {"workload": WORKLOAD, "seed": 0, "weight_copies": copies,
                    "l2": f"inputs larger than L2: {copies} rotating weight copies of "
                          f"{N * K / 1e6:.1f} MB", "graph": use_graph,
-                   "bytes_per_step": nbytes},
+                   "bytes_per_step_per_gpu": nbytes,
+                   "parallelism": "replicas (one lm_head GEMV stream per GPU)" if world > 1
+                   else "single GPU"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": UNIT,
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                     "traffic": traffic},
+                     "traffic": traffic, "per": "one GPU"},
         "e2e": e2e,
         "cpu_baseline": cpu,
-        "clocks": clk.summary(),
+        "clocks": clk.summary() if clk else None,
         "gpu_launches": args.steps,
-        "secondary": {"mlp_body": mlp},
+        "secondary": {"mlp_body": mlp, "tensor_parallel": tp},
     }
 
 
@@ -408,6 +504,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-mlp", action="store_true")
+    ap.add_argument("--no-tp", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=500)
     ap.add_argument("--cpu-reps", type=int, default=30)
     args = ap.parse_args()
@@ -415,14 +512,38 @@ def main():
         args.warmup = 3
 
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
     if args.impl == "reference":
         if rank != 0:
             return
-        print(json.dumps(run_reference(args)))
+        print(json.dumps(run_reference(args)), flush=True)
         return
-    if args.gpus != 1:
-        raise SystemExit("multi-GPU bench not implemented yet")
-    print(json.dumps(run_ours(args)))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
+    # stdout carries exactly one JSON line: NCCL's own messages go to stderr
+    os.environ.setdefault("NCCL_DEBUG", "WARN")
+    os.environ["NCCL_DEBUG_FILE"] = "/dev/stderr"
+    import datetime
+    import torch
+    import torch.distributed as dist
+    torch.cuda.set_device(local)
+    if world > 1:
+        init = "env://"
+    else:
+        import socket
+        with socket.socket() as sk:
+            sk.bind(("127.0.0.1", 0))
+            init = f"tcp://127.0.0.1:{sk.getsockname()[1]}"
+    dist.init_process_group("nccl", init_method=init, rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=300),
+                            device_id=torch.device("cuda", local))
+    try:
+        result = run_ours(args, rank, world, local)
+        if rank == 0:
+            print(json.dumps(result), flush=True)
+    finally:
+        dist.destroy_process_group()
 
 
 if __name__ == "__main__":
