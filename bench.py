@@ -327,17 +327,33 @@ def run_tp(args, rank: int, world: int, dev) -> dict:
         for _ in range(3):
             step()
         _barrier(world)
-        steps = 10
+        # The whole step -- kernels and NCCL collectives -- as one CUDA graph.
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            step()
+        torch.cuda.current_stream().wait_stream(side)
+        _barrier(world)
+        with torch.cuda.graph(graph):
+            step()
+        _barrier(world)
+        for _ in range(3):
+            graph.replay()
+        _barrier(world)
+        steps = 20
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record()
         for _ in range(steps):
-            step()
+            graph.replay()
         t1.record()
         _barrier(world)
         ms = _dist_max(t0.elapsed_time(t1) / steps, world)
         out[f"M{M}"] = {"ms_per_step": round(ms, 4), "tok_per_s": round(M / (ms * 1e-3), 1),
                         "weight_GBs": round(weight_bytes / (ms * 1e-3) / 1e9, 1)}
+        del graph      # a graph holding NCCL calls must go before the process group
+        torch.cuda.synchronize()
     del layers, head
     torch.cuda.empty_cache()
     return out
@@ -521,9 +537,10 @@ def main():
         return
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch N>1 with torchrun")
-    # stdout carries exactly one JSON line: NCCL's own messages go to stderr
-    os.environ.setdefault("NCCL_DEBUG", "WARN")
-    os.environ["NCCL_DEBUG_FILE"] = "/dev/stderr"
+    # stdout carries exactly one JSON line: anything a library prints to fd 1
+    # (NCCL's version banner, for one) goes to stderr while we run
+    real_stdout = os.dup(1)
+    os.dup2(2, 1)
     import datetime
     import torch
     import torch.distributed as dist
@@ -541,7 +558,8 @@ def main():
     try:
         result = run_ours(args, rank, world, local)
         if rank == 0:
-            print(json.dumps(result), flush=True)
+            sys.stdout.flush()
+            os.write(real_stdout, (json.dumps(result) + "\n").encode())
     finally:
         dist.destroy_process_group()
 
