@@ -143,6 +143,60 @@ int qz_fused_mlp_decode_noalloc(const int8_t* gu_q, const float* gu_s, int64_t n
  */
 int qz_silu_mul(const float* gu, float* a, int64_t M, int64_t I, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Decode-step glue: the fp32 work quartz's decoder does around its int8
+ * matmuls, so a whole token can run on the device (and in one CUDA graph).
+ * ------------------------------------------------------------------------ */
+
+/* out[m, :] = dequant(q[ids[m], :]) -- the int8 embedding gather
+ * (quartz/quantize.py:78-80 with dequantize_symmetric, 41-48). ids: device int64 [M]. */
+int qz_embed_gather(const int8_t* q, const float* scale, int64_t ng, const int64_t* ids,
+                    int64_t M, int64_t V, int64_t H, float* out, void* stream);
+
+/* y[r, :] = x[r, :] / sqrt(mean(x[r, :]^2) + eps) * w  (quartz/ops.py:24-32). */
+int qz_rmsnorm(const float* x, const float* w, float* y, int64_t rows, int64_t n, float eps,
+               void* stream);
+
+/*
+ * qkv [M, (nq + 2 nkv) * hd] -> q_out [M, nq * hd] and the KV cache
+ * ([nkv, max_ctx, hd] per layer) at positions pos0 + m: optional per-head
+ * RMSNorm of q and k (Qwen3, quartz/models/qwen3.py:33-34; pass NULL weights
+ * for Llama), half-split RoPE with the given inverse frequencies
+ * (quartz/rope.py:47-78), K/V append (quartz/cache.py:26-46). pos_dev, if
+ * not NULL, is a device int64 that replaces pos0 (for graph replay).
+ */
+int qz_qk_rope(const float* qkv, const float* q_norm_w, const float* k_norm_w,
+               const float* inv_freq, float* q_out, float* k_cache, float* v_cache, int64_t M,
+               int nq, int nkv, int hd, int64_t max_ctx, int64_t pos0, const int64_t* pos_dev,
+               float eps, void* stream);
+
+/* Workspace bytes qz_attention_decode needs for contexts up to max_ctx. */
+int qz_attention_decode_workspace_bytes(int nq, int hd, int64_t max_ctx, int64_t* bytes);
+
+/*
+ * One query row per head over the first T cache positions:
+ * out[h] = softmax(q[h] . K^T * scale) V, kv head h / (nq / nkv) (GQA by
+ * repeat, quartz/attention.py:29-43). T_dev, if not NULL, replaces T with
+ * *T_dev + t_offset (for graph replay).
+ */
+int qz_attention_decode(const float* q, const float* k_cache, const float* v_cache, float* out,
+                        int nq, int nkv, int hd, int64_t max_ctx, int64_t T, const int64_t* T_dev,
+                        int64_t t_offset, float scale, void* ws, size_t ws_bytes, void* stream);
+
+/* M query rows at positions pos0 .. pos0 + M - 1, each attending causally to
+ * cache positions 0 .. its own (the additive mask of quartz/attention.py:15-26). */
+int qz_attention_prefill(const float* q, const float* k_cache, const float* v_cache, float* out,
+                         int64_t M, int nq, int nkv, int hd, int64_t max_ctx, int64_t pos0,
+                         float scale, void* stream);
+
+/*
+ * tokens[m] = argmax of logits[m, :V], first index on ties (np.argmax,
+ * quartz/sample.py:21-22). keys: device uint64 [M], zero before the first
+ * call (left zero afterwards). pos_dev, if not NULL, is advanced by pos_step.
+ */
+int qz_argmax(const float* logits, int64_t M, int64_t V, uint64_t* keys, int64_t* tokens,
+              int64_t* pos_dev, int64_t pos_step, void* stream);
+
 /* Read the device status word of the current device into words[0..3]
  * ({error bits, first error site, block of first error, error count}); when
  * clear != 0 reset it to zero afterwards. Synchronises the device. */

@@ -36,6 +36,16 @@ SIGNATURES = {
     "qz_fused_mlp_decode_noalloc": ([_vp, _vp, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64,
                                      _vp], _int),
     "qz_silu_mul": ([_vp, _vp, _i64, _i64, _vp], _int),
+    "qz_embed_gather": ([_vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _vp], _int),
+    "qz_rmsnorm": ([_vp, _vp, _vp, _i64, _i64, ctypes.c_float, _vp], _int),
+    "qz_qk_rope": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _i64, _i64, _vp,
+                    ctypes.c_float, _vp], _int),
+    "qz_attention_decode_workspace_bytes": ([_int, _int, _i64, ctypes.POINTER(_i64)], _int),
+    "qz_attention_decode": ([_vp, _vp, _vp, _vp, _int, _int, _int, _i64, _i64, _vp, _i64,
+                             ctypes.c_float, _vp, ctypes.c_size_t, _vp], _int),
+    "qz_attention_prefill": ([_vp, _vp, _vp, _vp, _i64, _int, _int, _int, _i64, _i64,
+                              ctypes.c_float, _vp], _int),
+    "qz_argmax": ([_vp, _i64, _i64, _vp, _vp, _vp, _i64, _vp], _int),
     "qz_device_status": ([ctypes.POINTER(ctypes.c_uint32), _int], _int),
     "qz_sync": ([_vp], _int),
 }

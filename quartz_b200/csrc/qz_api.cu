@@ -13,6 +13,7 @@
 #include "qz_generic.cuh"
 #include "qz_stream.cuh"
 #include "qz_tc_gemm.cuh"
+#include "qz_decode.cuh"
 
 namespace {
 
@@ -554,6 +555,137 @@ int qz_fused_mlp_decode_noalloc(const int8_t* gu_q, const float* gu_s, int64_t n
   QZ_CUDA(cudaMemsetAsync(barrier, 0, sizeof(uint32_t), static_cast<cudaStream_t>(stream)));
   return qz_fused_mlp_decode(gu_q, gu_s, ng, x, down_q, down_s, ngd, scratch, out, residual, H, I,
                              barrier, stream);
+}
+
+
+// ---------------------------------------------------------------------------
+// decode-step glue (device pointers; stream-ordered)
+// ---------------------------------------------------------------------------
+int qz_embed_gather(const int8_t* q, const float* scale, int64_t ng, const int64_t* ids,
+                    int64_t M, int64_t V, int64_t H, float* out, void* stream) {
+  if (int rc = check_weights(q, scale, ng, V, H, "qz_embed_gather")) return rc;
+  if (M < 0) return fail(QZ_ERR_INVALID, "qz_embed_gather: negative M");
+  if (M == 0 || H == 0) return QZ_OK;
+  if (!ids || !out || V < 1) return fail(QZ_ERR_INVALID, "qz_embed_gather: null ids/out or empty table");
+  qz::dec::embed_gather_kernel<<<static_cast<unsigned>(M), 256, 0,
+                                 static_cast<cudaStream_t>(stream)>>>(q, scale, ng, ids, V, H, out);
+  QZ_CUDA(cudaGetLastError());
+  return QZ_OK;
+}
+
+int qz_rmsnorm(const float* x, const float* w, float* y, int64_t rows, int64_t n, float eps,
+               void* stream) {
+  if (rows < 0 || n < 0) return fail(QZ_ERR_INVALID, "qz_rmsnorm: negative size");
+  if (rows == 0 || n == 0) return QZ_OK;
+  if (!x || !w || !y) return fail(QZ_ERR_INVALID, "qz_rmsnorm: null pointer");
+  qz::dec::rmsnorm_kernel<<<static_cast<unsigned>(rows), 256, 0,
+                            static_cast<cudaStream_t>(stream)>>>(x, w, y, n, eps);
+  QZ_CUDA(cudaGetLastError());
+  return QZ_OK;
+}
+
+}  // extern "C"
+
+namespace {
+int check_heads(int nq, int nkv, int hd, const char* what) {
+  if (nq < 1 || nkv < 1 || nq % nkv)
+    return fail(QZ_ERR_INVALID, std::string(what) + ": query heads must be a multiple of kv heads");
+  if (hd < 2 || hd % 2 || hd > 256)
+    return fail(QZ_ERR_INVALID, std::string(what) + ": head_dim must be even and <= 256");
+  if (nq / nkv > 8) return fail(QZ_ERR_INVALID, std::string(what) + ": at most 8 query heads per kv head");
+  return QZ_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int qz_qk_rope(const float* qkv, const float* q_norm_w, const float* k_norm_w,
+               const float* inv_freq, float* q_out, float* k_cache, float* v_cache, int64_t M,
+               int nq, int nkv, int hd, int64_t max_ctx, int64_t pos0, const int64_t* pos_dev,
+               float eps, void* stream) {
+  if (int rc = check_heads(nq, nkv, hd, "qz_qk_rope")) return rc;
+  if (M < 0 || max_ctx < 1) return fail(QZ_ERR_INVALID, "qz_qk_rope: bad M or max_ctx");
+  if (M == 0) return QZ_OK;
+  if (!qkv || !inv_freq || !q_out || !k_cache || !v_cache)
+    return fail(QZ_ERR_INVALID, "qz_qk_rope: null pointer");
+  if (!pos_dev && (pos0 < 0 || pos0 + M > max_ctx))
+    return fail(QZ_ERR_INVALID, "qz_qk_rope: positions beyond the cache");
+  const dim3 grid(static_cast<unsigned>(M), static_cast<unsigned>(nq + 2 * nkv));
+  qz::dec::qk_rope_kernel<<<grid, 128, hd * sizeof(float), static_cast<cudaStream_t>(stream)>>>(
+      qkv, q_norm_w, k_norm_w, inv_freq, q_out, k_cache, v_cache, nq, nkv, hd, max_ctx, pos0,
+      pos_dev, eps);
+  QZ_CUDA(cudaGetLastError());
+  return QZ_OK;
+}
+
+int qz_attention_decode_workspace_bytes(int nq, int hd, int64_t max_ctx, int64_t* bytes) {
+  if (!bytes || nq < 1 || hd < 1 || max_ctx < 1)
+    return fail(QZ_ERR_INVALID, "qz_attention_decode_workspace_bytes: bad arguments");
+  *bytes = static_cast<int64_t>(nq) * qz::cdiv(max_ctx, qz::dec::kChunk) * (hd + 2) * 4;
+  return QZ_OK;
+}
+
+int qz_attention_decode(const float* q, const float* k_cache, const float* v_cache, float* out,
+                        int nq, int nkv, int hd, int64_t max_ctx, int64_t T, const int64_t* T_dev,
+                        int64_t t_offset, float scale, void* ws, size_t ws_bytes, void* stream) {
+  if (int rc = check_heads(nq, nkv, hd, "qz_attention_decode")) return rc;
+  if (max_ctx < 1) return fail(QZ_ERR_INVALID, "qz_attention_decode: bad max_ctx");
+  if (!T_dev && (T < 1 || T > max_ctx))
+    return fail(QZ_ERR_INVALID, "qz_attention_decode: context length outside [1, max_ctx]");
+  if (!q || !k_cache || !v_cache || !out || !ws)
+    return fail(QZ_ERR_INVALID, "qz_attention_decode: null pointer");
+  // With the length in device memory every chunk of the cache gets a block.
+  const int64_t span = T_dev ? max_ctx : T;
+  const int64_t nchunks = qz::cdiv(span, qz::dec::kChunk);
+  const int64_t need = static_cast<int64_t>(nq) * nchunks * (hd + 2) * 4;
+  if (static_cast<int64_t>(ws_bytes) < need)
+    return fail(QZ_ERR_INVALID, "qz_attention_decode: workspace too small");
+  float* part = static_cast<float*>(ws);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int n_rep = nq / nkv;
+  const int smem = (n_rep * hd + n_rep * qz::dec::kChunk) * 4;
+  const dim3 grid(static_cast<unsigned>(nkv), static_cast<unsigned>(nchunks));
+  qz::dec::attn_decode_kernel<<<grid, 256, smem, st>>>(q, k_cache, v_cache, part, nq, nkv, hd,
+                                                       max_ctx, T, T_dev, t_offset, scale);
+  QZ_CUDA(cudaGetLastError());
+  qz::dec::attn_combine_kernel<<<static_cast<unsigned>(nq), 128, 0, st>>>(
+      part, out, hd, static_cast<int>(nchunks));
+  QZ_CUDA(cudaGetLastError());
+  return QZ_OK;
+}
+
+int qz_attention_prefill(const float* q, const float* k_cache, const float* v_cache, float* out,
+                         int64_t M, int nq, int nkv, int hd, int64_t max_ctx, int64_t pos0,
+                         float scale, void* stream) {
+  if (int rc = check_heads(nq, nkv, hd, "qz_attention_prefill")) return rc;
+  if (M < 0 || pos0 < 0 || pos0 + M > max_ctx)
+    return fail(QZ_ERR_INVALID, "qz_attention_prefill: positions beyond the cache");
+  if (M == 0) return QZ_OK;
+  if (!q || !k_cache || !v_cache || !out) return fail(QZ_ERR_INVALID, "qz_attention_prefill: null pointer");
+  const int64_t warps = M * nq;
+  const unsigned blocks = static_cast<unsigned>(qz::cdiv(warps * 32, 256));
+  qz::dec::attn_prefill_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      q, k_cache, v_cache, out, M, nq, nkv, hd, max_ctx, pos0, scale);
+  QZ_CUDA(cudaGetLastError());
+  return QZ_OK;
+}
+
+int qz_argmax(const float* logits, int64_t M, int64_t V, uint64_t* keys, int64_t* tokens,
+              int64_t* pos_dev, int64_t pos_step, void* stream) {
+  if (M < 0 || V < 1 || V > 0xFFFFFFFFll) return fail(QZ_ERR_INVALID, "qz_argmax: bad sizes");
+  if (M == 0) return QZ_OK;
+  if (!logits || !keys || !tokens) return fail(QZ_ERR_INVALID, "qz_argmax: null pointer");
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const unsigned bx = static_cast<unsigned>(std::min<int64_t>(qz::cdiv(V, 1024), d->sms));
+  qz::dec::argmax_kernel<<<dim3(bx, static_cast<unsigned>(M)), 256, 0, st>>>(
+      logits, V, reinterpret_cast<unsigned long long*>(keys));
+  QZ_CUDA(cudaGetLastError());
+  qz::dec::argmax_finish_kernel<<<static_cast<unsigned>(qz::cdiv(M, 128)), 128, 0, st>>>(
+      reinterpret_cast<unsigned long long*>(keys), tokens, M, pos_dev, pos_step);
+  QZ_CUDA(cudaGetLastError());
+  return QZ_OK;
 }
 
 int qz_silu_mul(const float* gu, float* a, int64_t M, int64_t I, void* stream) {

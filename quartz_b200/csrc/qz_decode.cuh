@@ -1,0 +1,315 @@
+// qz_decode.cuh -- the device-side glue of an all-int8 decode step around the
+// int8 matmuls: everything quartz's decoder does between its QuantizedLinear
+// calls, so a whole token can run on the GPU (and inside one CUDA graph).
+//
+//   embed_gather_kernel   int8 embedding row gather + dequant    quartz/quantize.py:78-80, 41-48
+//   rmsnorm_kernel        x / sqrt(mean(x^2) + eps) * w          quartz/ops.py:24-32
+//   qk_rope_kernel        per-head q/k RMSNorm (Qwen3), half-split
+//                         RoPE, K/V append to the cache          quartz/models/qwen3.py:31-41,
+//                                                                quartz/rope.py:47-78,
+//                                                                quartz/cache.py:26-46
+//   attn_decode_kernel +  one query per head over the cache,     quartz/attention.py:29-43
+//   attn_combine_kernel   context split in chunks, GQA by repeat
+//   attn_prefill_kernel   M queries, causal, online softmax       quartz/attention.py:15-43
+//   argmax_kernel         greedy token, first index of the max   quartz/sample.py:21-22
+//
+// All arithmetic is fp32 like the reference. Layouts: activations row-major
+// [M, features]; the KV cache of one layer is [n_kv, max_ctx, head_dim].
+#pragma once
+
+#include "qz_device.cuh"
+
+namespace qz {
+namespace dec {
+
+__device__ __forceinline__ float warp_sum_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max_f(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide sum for blockDim.x <= 1024 (every thread gets the result).
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum_f(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = (blockDim.x + 31) >> 5;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float s = 0.f;
+  for (int i = 0; i < nw; ++i) s += red[i];
+  return s;
+}
+
+// out[m, h] = (float)q[id_m, h] * scale[id_m, h / G]
+__global__ void embed_gather_kernel(const int8_t* __restrict__ q, const float* __restrict__ scale,
+                                    int64_t ng, const int64_t* __restrict__ ids, int64_t V,
+                                    int64_t H, float* __restrict__ out) {
+  const int64_t m = blockIdx.x;
+  int64_t id = ids[m];
+  id = id < 0 ? 0 : (id >= V ? V - 1 : id);   // ids are validated on the host; stay in bounds
+  const int64_t G = H / ng;
+  for (int64_t h = threadIdx.x; h < H; h += blockDim.x)
+    out[m * H + h] = static_cast<float>(q[id * H + h]) * scale[id * ng + h / G];
+}
+
+// One block per row: y = x * (1 / sqrt(mean(x^2) + eps)) * w.
+__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
+                               float* __restrict__ y, int64_t n, float eps) {
+  __shared__ float red[32];
+  const float* xr = x + blockIdx.x * n;
+  float ss = 0.f;
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+  ss = block_sum(ss, red);
+  const float r = 1.0f / sqrtf(ss / static_cast<float>(n) + eps);
+  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) y[blockIdx.x * n + i] = xr[i] * r * w[i];
+}
+
+// qkv: [M, (nq + 2 nkv) * hd] (q heads, k heads, v heads). One block per
+// (row m, head): q and k heads get the optional per-head RMSNorm then RoPE at
+// position pos0 + m; q goes to q_out [M, nq * hd], k and v to the cache.
+// pos_dev (if not null) overrides pos0: the position read from device memory,
+// so a captured graph can be replayed at successive positions.
+__global__ void qk_rope_kernel(const float* __restrict__ qkv, const float* __restrict__ qn_w,
+                               const float* __restrict__ kn_w, const float* __restrict__ inv_freq,
+                               float* __restrict__ q_out, float* __restrict__ kc,
+                               float* __restrict__ vc, int nq, int nkv, int hd, int64_t max_ctx,
+                               int64_t pos0, const int64_t* __restrict__ pos_dev, float eps) {
+  extern __shared__ float sh[];   // hd floats
+  __shared__ float red[32];
+  const int64_t m = blockIdx.x;
+  const int head = blockIdx.y;
+  const int width = (nq + 2 * nkv) * hd;
+  const float* src = qkv + m * width + head * hd;
+  const int64_t pos = (pos_dev ? *pos_dev : pos0) + m;
+  if (pos < 0 || pos >= max_ctx) return;   // the host checks; never write outside the cache
+  const bool is_q = head < nq, is_k = !is_q && head < nq + nkv;
+  if (!is_q && !is_k) {   // v head: copy into the cache
+    const int vh = head - nq - nkv;
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) vc[(vh * max_ctx + pos) * hd + i] = src[i];
+    return;
+  }
+  const float* nw = is_q ? qn_w : kn_w;
+  for (int i = threadIdx.x; i < hd; i += blockDim.x) sh[i] = src[i];
+  if (nw) {
+    float ss = 0.f;
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) ss = fmaf(src[i], src[i], ss);
+    ss = block_sum(ss, red);
+    const float r = 1.0f / sqrtf(ss / static_cast<float>(hd) + eps);
+    __syncthreads();
+    for (int i = threadIdx.x; i < hd; i += blockDim.x) sh[i] = src[i] * r * nw[i];
+  }
+  __syncthreads();
+  const int d = hd / 2;
+  float* dst = is_q ? q_out + (m * nq + head) * hd
+                    : kc + ((head - nq) * max_ctx + pos) * hd;
+  const float fpos = static_cast<float>(pos);
+  for (int j = threadIdx.x; j < d; j += blockDim.x) {
+    const float ang = fpos * inv_freq[j];
+    const float c = cosf(ang), s = sinf(ang);
+    const float x1 = sh[j], x2 = sh[j + d];
+    dst[j] = x1 * c - x2 * s;
+    dst[j + d] = x2 * c + x1 * s;
+  }
+}
+
+// Decode attention, one query per head. Block (kv head g, chunk c) covers cache
+// positions [c*C, min(T, (c+1)*C)) for the n_rep query heads g*n_rep .. g*n_rep
+// + n_rep - 1 (quartz repeats each kv head to n_rep adjacent query heads). It
+// writes, per query head, the chunk's max score, sum of exp and exp-weighted
+// V sum; attn_combine_kernel merges the chunks.
+// part layout: [nq][nchunks][hd + 2]  (acc[hd], max, sum)
+// T_dev (if not null) overrides T (context length read from device memory);
+// chunks at or past T write empty partials.
+constexpr int kChunk = 64;
+__global__ void __launch_bounds__(256) attn_decode_kernel(
+    const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+    float* __restrict__ part, int nq, int nkv, int hd, int64_t max_ctx, int64_t T,
+    const int64_t* __restrict__ T_dev, int64_t t_offset, float scale) {
+  extern __shared__ float sm[];
+  const int g = blockIdx.x, c = blockIdx.y;
+  const int n_rep = nq / nkv;
+  const int nchunks = gridDim.y;
+  float* qs = sm;                        // [n_rep][hd]
+  float* ps = qs + n_rep * hd;           // [n_rep][kChunk] scores -> probabilities
+  if (T_dev) T = *T_dev + t_offset;
+  T = T > max_ctx ? max_ctx : T;
+  const int64_t t0 = static_cast<int64_t>(c) * kChunk;
+  const int nt = static_cast<int>(min64(kChunk, T - t0));
+  if (nt <= 0) {
+    for (int i = threadIdx.x; i < n_rep * (hd + 2); i += blockDim.x) {
+      const int r = i / (hd + 2), j = i - r * (hd + 2);
+      float* pr = part + ((static_cast<int64_t>(g * n_rep + r) * nchunks + c) * (hd + 2));
+      pr[j] = j == hd ? -INFINITY : 0.f;
+    }
+    return;
+  }
+  for (int i = threadIdx.x; i < n_rep * hd; i += blockDim.x) qs[i] = q[g * n_rep * hd + i];
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const float* kg = kc + (static_cast<int64_t>(g) * max_ctx) * hd;
+  const float* vg = vc + (static_cast<int64_t>(g) * max_ctx) * hd;
+  for (int t = warp; t < nt; t += nw) {
+    const float* kr = kg + (t0 + t) * hd;
+    for (int r = 0; r < n_rep; ++r) {
+      float s = 0.f;
+      for (int i = lane; i < hd; i += 32) s = fmaf(qs[r * hd + i], kr[i], s);
+      s = warp_sum_f(s);
+      if (lane == 0) ps[r * kChunk + t] = s * scale;
+    }
+  }
+  __syncthreads();
+  __shared__ float mx_s[32], sum_s[32];
+  if (warp < n_rep) {
+    float m = -INFINITY;
+    for (int t = lane; t < nt; t += 32) m = fmaxf(m, ps[warp * kChunk + t]);
+    m = warp_max_f(m);
+    float sum = 0.f;
+    for (int t = lane; t < nt; t += 32) {
+      const float e = expf(ps[warp * kChunk + t] - m);
+      ps[warp * kChunk + t] = e;
+      sum += e;
+    }
+    sum = warp_sum_f(sum);
+    if (lane == 0) { mx_s[warp] = m; sum_s[warp] = sum; }
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < n_rep * hd; i += blockDim.x) {
+    const int r = i / hd, dd = i - r * hd;
+    float acc = 0.f;
+    for (int t = 0; t < nt; ++t) acc = fmaf(ps[r * kChunk + t], vg[(t0 + t) * hd + dd], acc);
+    float* pr = part + ((static_cast<int64_t>(g * n_rep + r) * nchunks + c) * (hd + 2));
+    pr[dd] = acc;
+    if (dd == 0) { pr[hd] = mx_s[r]; pr[hd + 1] = sum_s[r]; }
+  }
+}
+
+// out[h, d] = sum_c exp(m_c - M) acc_c[d] / sum_c exp(m_c - M) l_c  (one block per query head)
+__global__ void attn_combine_kernel(const float* __restrict__ part, float* __restrict__ out,
+                                    int hd, int nchunks) {
+  const int h = blockIdx.x;
+  const float* ph = part + static_cast<int64_t>(h) * nchunks * (hd + 2);
+  float M = -INFINITY;
+  for (int c = 0; c < nchunks; ++c) M = fmaxf(M, ph[c * (hd + 2) + hd]);
+  float den = 0.f;
+  for (int c = 0; c < nchunks; ++c) {
+    const float mc = ph[c * (hd + 2) + hd];
+    if (mc != -INFINITY) den += expf(mc - M) * ph[c * (hd + 2) + hd + 1];
+  }
+  for (int d = threadIdx.x; d < hd; d += blockDim.x) {
+    float num = 0.f;
+    for (int c = 0; c < nchunks; ++c) {
+      const float mc = ph[c * (hd + 2) + hd];
+      if (mc != -INFINITY) num += expf(mc - M) * ph[c * (hd + 2) + d];
+    }
+    out[static_cast<int64_t>(h) * hd + d] = num / den;
+  }
+}
+
+// Prefill attention: query rows m (position pos0 + m) attend to cache positions
+// [0, pos0 + m] (causal). One warp per (row m, query head); online softmax
+// over the keys; hd <= 256.
+__global__ void __launch_bounds__(256) attn_prefill_kernel(
+    const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+    float* __restrict__ out, int64_t M, int nq, int nkv, int hd, int64_t max_ctx, int64_t pos0,
+    float scale) {
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  if (wid >= M * nq) return;
+  const int64_t m = wid / nq;
+  const int h = static_cast<int>(wid - m * nq);
+  const int g = h / (nq / nkv);
+  const int per = (hd + 31) / 32;   // <= 8
+  float qv[8], acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int i = lane + 32 * j;
+    qv[j] = (j < per && i < hd) ? q[(m * nq + h) * hd + i] : 0.f;
+    acc[j] = 0.f;
+  }
+  const float* kg = kc + static_cast<int64_t>(g) * max_ctx * hd;
+  const float* vg = vc + static_cast<int64_t>(g) * max_ctx * hd;
+  float mrun = -INFINITY, lrun = 0.f;
+  const int64_t T = pos0 + m + 1;
+  for (int64_t t = 0; t < T; ++t) {
+    float s = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = lane + 32 * j;
+      if (j < per && i < hd) s = fmaf(qv[j], kg[t * hd + i], s);
+    }
+    s = warp_sum_f(s) * scale;
+    const float mnew = fmaxf(mrun, s);
+    const float corr = expf(mrun - mnew);
+    const float p = expf(s - mnew);
+    lrun = lrun * corr + p;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int i = lane + 32 * j;
+      if (j < per && i < hd) acc[j] = acc[j] * corr + p * vg[t * hd + i];
+    }
+    mrun = mnew;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int i = lane + 32 * j;
+    if (j < per && i < hd) out[(m * nq + h) * hd + i] = acc[j] / lrun;
+  }
+}
+
+// Greedy argmax of each row of logits [M, V]: a block reduces a slice of a row
+// to one packed key (order-preserving float bits << 32 | ~index) and
+// atomicMax-es it into keys[m] (zeroed before); larger value wins, then the
+// lower index, as np.argmax.
+__device__ __forceinline__ unsigned long long pack_key(float v, int64_t idx) {
+  const uint32_t b = __float_as_uint(v);
+  const uint32_t ord = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return (static_cast<unsigned long long>(ord) << 32) |
+         (0xFFFFFFFFull - static_cast<unsigned long long>(idx));
+}
+
+__global__ void argmax_kernel(const float* __restrict__ logits, int64_t V,
+                              unsigned long long* __restrict__ keys) {
+  __shared__ unsigned long long red[32];
+  const int64_t m = blockIdx.y;
+  const float* row = logits + m * V;
+  unsigned long long best = 0ull;
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < V;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const unsigned long long k = pack_key(row[i], i);
+    best = k > best ? k : best;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const unsigned long long other = __shfl_xor_sync(0xffffffffu, best, o);
+    best = other > best ? other : best;
+  }
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) red[w] = best;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int i = 1; i < static_cast<int>(blockDim.x >> 5); ++i) best = red[i] > best ? red[i] : best;
+    best = red[0] > best ? red[0] : best;
+    atomicMax(keys + m, best);
+  }
+}
+
+// token[m] = index packed in keys[m]; keys reset to 0 for the next call.
+// If pos_dev is set, thread 0 also advances that position counter by `step`.
+__global__ void argmax_finish_kernel(unsigned long long* __restrict__ keys,
+                                     int64_t* __restrict__ tokens, int64_t M,
+                                     int64_t* __restrict__ pos_dev, int64_t step) {
+  const int64_t m = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (m < M) {
+    tokens[m] = static_cast<int64_t>(0xFFFFFFFFull - (keys[m] & 0xFFFFFFFFull));
+    keys[m] = 0ull;
+  }
+  if (pos_dev && m == 0) *pos_dev += step;
+}
+
+}  // namespace dec
+}  // namespace qz

@@ -1,0 +1,377 @@
+"""All-int8 greedy decoding on one GPU: the device decode step around the int8 path.
+
+quartz decodes with numpy on the host (quartz/generate.py:36-58): per token,
+embedding gather -> per layer [RMSNorm -> q/k/v projections -> (Qwen3) q/k
+RMSNorm -> RoPE -> KV append -> GQA attention -> o projection + residual ->
+RMSNorm -> fused int8 MLP + residual] -> final RMSNorm -> lm_head -> argmax
+(quartz/models/common.py:29-78, quartz/models/qwen3.py:31-45). ``DecodeEngine``
+runs every one of those steps as a kernel of libquartz_b200 on device-resident
+weights and KV cache, so a whole token is stream-ordered device work with no
+host round trip, and ``generate`` replays it from a CUDA graph: the position
+counter and the token live in device memory, the argmax kernel writes the
+next token where the embedding gather of the next replay reads it, and the
+only host traffic is the final token list.
+
+Differences of form (not of results) from quartz:
+* q, k and v are one stacked [(nq + 2 nkv) hd, H] int8 matrix (one GEMV
+  instead of three; rows and scales are the three matrices' own);
+* the KV cache is preallocated [layers, n_kv, max_ctx, head_dim] fp32 instead
+  of growing in 256-position steps (quartz/cache.py:26-46);
+* prefill (M > 1) runs the tensor-core int8 GEMM and the causal prefill
+  attention, decode (M = 1) the streaming GEMVs and the fused MLP, the same
+  M split as quartz/quantize.py:99-114.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Iterable, Mapping
+
+import numpy as np
+import torch
+
+from . import _lib, device as qd
+from .model import ModelSpec, rope_inv_freq
+
+
+def _dev_f32(a, dev) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(dev)
+
+
+def _dev_i8(a, dev) -> torch.Tensor:
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.int8)).to(dev)
+
+
+class _Layer:
+    __slots__ = ("qkv_q", "qkv_s", "o_q", "o_s", "gu_q", "gu_s", "down_q", "down_s", "in_w",
+                 "post_w", "qn_w", "kn_w")
+
+
+class DecodeEngine:
+    """Device-resident all-int8 decoder for one sequence.
+
+    weights: name -> (q int8 [out, in], scale fp32 [out, ng]) for every Linear
+    and the embedding (names as quartz.model.leaf_names), name -> fp32 vector for
+    the RMSNorms (quartz.model.norm_weights). Iterables of (name, q, scale) are
+    accepted for the int8 tensors so a large checkpoint streams to the device.
+    """
+
+    def __init__(self, spec: ModelSpec, int8_weights: Mapping | Iterable, norms: Mapping,
+                 *, max_ctx: int, max_prefill: int = 512, device=None):
+        self.spec = spec
+        self.dev = torch.device("cuda", qd.ensure_device(device))
+        dev = self.dev
+        self.lib = _lib.load()
+        self.max_ctx = int(max_ctx)
+        self.max_prefill = max(1, int(max_prefill))
+        S = spec
+        H, hd = S.hidden, S.head_dim
+        self.layers = [_Layer() for _ in range(S.layers)]
+        self.embed_q = self.embed_s = self.lm_q = self.lm_s = None
+        leaves = ("q_proj", "k_proj", "v_proj", "o_proj", "gate_proj", "up_proj", "down_proj")
+        pending: dict[int, dict[str, tuple]] = {}
+
+        def upload_layer(i: int, w: dict) -> None:
+            L = self.layers[i]
+            if len({w[n][1].shape[1] for n in ("q_proj", "k_proj", "v_proj")}) != 1:
+                raise ValueError("q/k/v scales must share a group count")
+            L.qkv_q = _dev_i8(np.concatenate([w[n][0] for n in ("q_proj", "k_proj", "v_proj")]), dev)
+            L.qkv_s = _dev_f32(np.concatenate([w[n][1] for n in ("q_proj", "k_proj", "v_proj")]), dev)
+            L.o_q, L.o_s = _dev_i8(w["o_proj"][0], dev), _dev_f32(w["o_proj"][1], dev)
+            # gate rows over up rows, the layout of quartz/quantize.py:95-96
+            L.gu_q = _dev_i8(np.concatenate([w["gate_proj"][0], w["up_proj"][0]]), dev)
+            L.gu_s = _dev_f32(np.concatenate([w["gate_proj"][1], w["up_proj"][1]]), dev)
+            L.down_q, L.down_s = _dev_i8(w["down_proj"][0], dev), _dev_f32(w["down_proj"][1], dev)
+
+        pairs = ((n, *qs) for n, qs in int8_weights.items()) \
+            if isinstance(int8_weights, Mapping) else int8_weights
+        for name, q, s in pairs:
+            if name == "model.embed_tokens":
+                self.embed_q, self.embed_s = _dev_i8(q, dev), _dev_f32(s, dev)
+                continue
+            if name == "lm_head":
+                self.lm_q, self.lm_s = _dev_i8(q, dev), _dev_f32(s, dev)
+                continue
+            parts = name.split(".")
+            if (len(parts) != 5 or parts[:2] != ["model", "layers"] or parts[4] not in leaves
+                    or not 0 <= int(parts[2]) < S.layers):
+                raise KeyError(f"unexpected weight {name!r}")
+            i = int(parts[2])
+            w = pending.setdefault(i, {})
+            w[parts[4]] = (q, s)
+            if len(w) == len(leaves):      # layer complete: upload and drop the host copies
+                upload_layer(i, pending.pop(i))
+        if pending:
+            raise ValueError(f"incomplete weights for layers {sorted(pending)}")
+        if self.embed_q is None:
+            raise ValueError("missing model.embed_tokens")
+        if S.tie:
+            self.lm_q, self.lm_s = self.embed_q, self.embed_s
+        elif self.lm_q is None:
+            raise ValueError("missing lm_head (tie_word_embeddings is false)")
+        for i, L in enumerate(self.layers):
+            p = f"model.layers.{i}."
+            for attr in ("qkv_q", "o_q", "gu_q", "down_q"):
+                if not hasattr(L, attr):
+                    raise ValueError(f"layer {i} lacks {attr}")
+            L.in_w = _dev_f32(norms[p + "input_layernorm"], dev)
+            L.post_w = _dev_f32(norms[p + "post_attention_layernorm"], dev)
+            if S.qk_norm:
+                L.qn_w = _dev_f32(norms[p + "self_attn.q_norm"], dev)
+                L.kn_w = _dev_f32(norms[p + "self_attn.k_norm"], dev)
+            else:
+                L.qn_w = L.kn_w = None
+        self.norm_w = _dev_f32(norms["model.norm"], dev)
+        self.inv_freq = _dev_f32(rope_inv_freq(S), dev)
+        self.attn_scale = float(hd ** -0.5)
+        self.ng = self.layers[0].qkv_s.shape[1] if self.layers else 1
+
+        # KV cache and activation buffers
+        f32 = dict(dtype=torch.float32, device=dev)
+        self.k_cache = torch.zeros((S.layers, S.n_kv, self.max_ctx, hd), **f32)
+        self.v_cache = torch.zeros((S.layers, S.n_kv, self.max_ctx, hd), **f32)
+        Mx = self.max_prefill
+        self.h_a = torch.zeros((Mx, H), **f32)
+        self.h_b = torch.zeros((Mx, H), **f32)
+        self.xn = torch.zeros((Mx, H), **f32)
+        self.qkv = torch.zeros((Mx, S.qkv_rows), **f32)
+        self.qo = torch.zeros((Mx, S.n_heads * hd), **f32)
+        self.ao = torch.zeros((Mx, S.n_heads * hd), **f32)
+        self.gu = torch.zeros((Mx, 2 * S.inter), **f32) if Mx > 1 else None
+        self.act = torch.zeros((Mx, S.inter), **f32) if Mx > 1 else None
+        self.abuf = torch.zeros(S.inter, **f32)
+        self.logits = torch.zeros(S.vocab, **f32)
+        self.keys = torch.zeros(8, dtype=torch.int64, device=dev)
+        self.tok = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.ids = torch.zeros(Mx, dtype=torch.int64, device=dev)
+        self.pos_dev = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.pos = 0
+        self.mlp_ws = torch.zeros(self.lib.qz_mlp_workspace_bytes() // 4, dtype=torch.int32,
+                                  device=dev)
+        b = ctypes.c_int64(0)
+        _lib.check(self.lib.qz_attention_decode_workspace_bytes(S.n_heads, hd, self.max_ctx,
+                                                                ctypes.byref(b)))
+        self.attn_ws = torch.empty(b.value, dtype=torch.uint8, device=dev)
+        self.gemm_ws = None
+        if Mx > 1:
+            need = 0
+            for N, K in ((S.qkv_rows, H), (H, S.n_heads * hd), (2 * S.inter, H), (H, S.inter)):
+                b = ctypes.c_int64(0)
+                _lib.check(self.lib.qz_gemm_w8_workspace_bytes(Mx, N, K, ctypes.byref(b)))
+                need = max(need, b.value)
+            self.gemm_ws = torch.empty(need, dtype=torch.uint8, device=dev)
+        self._graph = None
+        self._graph_steps = 0
+
+    # ------------------------------------------------------------------ state
+    def reset(self, pos: int = 0) -> None:
+        """Forget the sequence: the next token is written at position `pos`."""
+        if not 0 <= pos <= self.max_ctx:
+            raise ValueError("position outside the cache")
+        self.pos = int(pos)
+        self.pos_dev.fill_(self.pos)
+
+    def load_kv(self, kv: Iterable) -> None:
+        """Fill the cache from per-layer (K, V) [n_kv, T, head_dim] arrays and set
+        the position to T (the prefilled-cache start, like calling quartz's
+        update_and_fetch once per layer, quartz/cache.py:26-46)."""
+        T = None
+        n = 0
+        for i, (k, v) in enumerate(kv):
+            k = torch.as_tensor(np.ascontiguousarray(k, np.float32))
+            v = torch.as_tensor(np.ascontiguousarray(v, np.float32))
+            t = k.shape[1]
+            if T is None:
+                T = t
+            if k.shape != (self.spec.n_kv, T, self.spec.head_dim) or v.shape != k.shape:
+                raise ValueError("K/V must be [n_kv, T, head_dim] with one T for all layers")
+            if T > self.max_ctx:
+                raise ValueError("prefilled context exceeds max_ctx")
+            self.k_cache[i, :, :T].copy_(k)
+            self.v_cache[i, :, :T].copy_(v)
+            n += 1
+        if n != self.spec.layers:
+            raise ValueError(f"expected K/V for {self.spec.layers} layers, got {n}")
+        self.reset(T)
+
+    # ------------------------------------------------------------- the token
+    def _stream(self) -> int:
+        return torch.cuda.current_stream(self.dev).cuda_stream
+
+    def _decode_ops(self, st: int) -> None:
+        """One token at position *pos_dev: reads self.tok, writes self.tok and
+        advances pos_dev. Every call is a libquartz_b200 launch on stream st."""
+        S, lib, chk = self.spec, self.lib, _lib.check
+        H, hd, nq, nkv = S.hidden, S.head_dim, S.n_heads, S.n_kv
+        p = lambda t: t.data_ptr()  # noqa: E731
+        h_a, h_b, xn = p(self.h_a), p(self.h_b), p(self.xn)
+        chk(lib.qz_embed_gather(p(self.embed_q), p(self.embed_s), self.embed_s.shape[1],
+                                p(self.tok), 1, S.vocab, H, h_a, st))
+        for li, L in enumerate(self.layers):
+            kc, vc = p(self.k_cache[li]), p(self.v_cache[li])
+            chk(lib.qz_rmsnorm(h_a, p(L.in_w), xn, 1, H, S.eps, st))
+            chk(lib.qz_gemv_w8(p(L.qkv_q), p(L.qkv_s), L.qkv_s.shape[1], xn, p(self.qkv),
+                               S.qkv_rows, H, None, st))
+            chk(lib.qz_qk_rope(p(self.qkv), qd._ptr(L.qn_w), qd._ptr(L.kn_w), p(self.inv_freq),
+                               p(self.qo), kc, vc, 1, nq, nkv, hd, self.max_ctx, 0,
+                               p(self.pos_dev), S.eps, st))
+            chk(lib.qz_attention_decode(p(self.qo), kc, vc, p(self.ao), nq, nkv, hd, self.max_ctx,
+                                        0, p(self.pos_dev), 1, self.attn_scale, p(self.attn_ws),
+                                        self.attn_ws.numel(), st))
+            chk(lib.qz_gemv_w8(p(L.o_q), p(L.o_s), L.o_s.shape[1], p(self.ao), h_b, H, nq * hd,
+                               h_a, st))
+            chk(lib.qz_rmsnorm(h_b, p(L.post_w), xn, 1, H, S.eps, st))
+            chk(lib.qz_fused_mlp_decode(p(L.gu_q), p(L.gu_s), L.gu_s.shape[1], xn, p(L.down_q),
+                                        p(L.down_s), L.down_s.shape[1], p(self.abuf), h_a, h_b,
+                                        H, S.inter, p(self.mlp_ws), st))
+        chk(lib.qz_rmsnorm(h_a, p(self.norm_w), xn, 1, H, S.eps, st))
+        chk(lib.qz_gemv_w8(p(self.lm_q), p(self.lm_s), self.lm_s.shape[1], xn, p(self.logits),
+                           S.vocab, H, None, st))
+        chk(lib.qz_argmax(p(self.logits), 1, S.vocab, p(self.keys), p(self.tok), p(self.pos_dev),
+                          1, st))
+
+    def _launches_per_token(self) -> int:
+        # embed + per layer (rmsnorm, qkv, rope, attn x2, o, rmsnorm, mlp) + norm, lm, argmax x2
+        return 1 + 8 * self.spec.layers + 4
+
+    def prefill(self, ids: Iterable[int]) -> int:
+        """Run the prompt ids at the current position; return the greedy next token
+        (quartz/generate.py:50 then quartz/models/common.py:69-78 on the last row)."""
+        ids = [int(t) for t in ids]
+        M = len(ids)
+        S = self.spec
+        if M == 0:
+            raise ValueError("empty prompt: nothing to prefill")
+        if any(t < 0 or t >= S.vocab for t in ids):
+            raise ValueError("token id outside the vocabulary")
+        if self.pos + M > self.max_ctx:
+            raise ValueError("prompt does not fit in the cache")
+        if M == 1:
+            return self.decode(ids[0])
+        if M > self.max_prefill:
+            raise ValueError(f"prompt of {M} tokens exceeds max_prefill={self.max_prefill}")
+        st = self._stream()
+        lib, chk = self.lib, _lib.check
+        H, hd, nq, nkv, I = S.hidden, S.head_dim, S.n_heads, S.n_kv, S.inter
+        p = lambda t: t.data_ptr()  # noqa: E731
+        self.ids[:M].copy_(torch.tensor(ids, dtype=torch.int64))
+        h_a, h_b, xn = p(self.h_a), p(self.h_b), p(self.xn)
+        ws, wsb = p(self.gemm_ws), self.gemm_ws.numel()
+        pos0 = self.pos
+        chk(lib.qz_embed_gather(p(self.embed_q), p(self.embed_s), self.embed_s.shape[1],
+                                p(self.ids), M, S.vocab, H, h_a, st))
+        for li, L in enumerate(self.layers):
+            kc, vc = p(self.k_cache[li]), p(self.v_cache[li])
+            chk(lib.qz_rmsnorm(h_a, p(L.in_w), xn, M, H, S.eps, st))
+            chk(lib.qz_gemm_w8_ws(p(L.qkv_q), p(L.qkv_s), L.qkv_s.shape[1], xn, p(self.qkv), M,
+                                  S.qkv_rows, H, None, ws, wsb, st))
+            chk(lib.qz_qk_rope(p(self.qkv), qd._ptr(L.qn_w), qd._ptr(L.kn_w), p(self.inv_freq),
+                               p(self.qo), kc, vc, M, nq, nkv, hd, self.max_ctx, pos0, None,
+                               S.eps, st))
+            chk(lib.qz_attention_prefill(p(self.qo), kc, vc, p(self.ao), M, nq, nkv, hd,
+                                         self.max_ctx, pos0, self.attn_scale, st))
+            chk(lib.qz_gemm_w8_ws(p(L.o_q), p(L.o_s), L.o_s.shape[1], p(self.ao), h_b, M, H,
+                                  nq * hd, h_a, ws, wsb, st))
+            chk(lib.qz_rmsnorm(h_b, p(L.post_w), xn, M, H, S.eps, st))
+            chk(lib.qz_gemm_w8_ws(p(L.gu_q), p(L.gu_s), L.gu_s.shape[1], xn, p(self.gu), M,
+                                  2 * I, H, None, ws, wsb, st))
+            chk(lib.qz_silu_mul(p(self.gu), p(self.act), M, I, st))
+            chk(lib.qz_gemm_w8_ws(p(L.down_q), p(L.down_s), L.down_s.shape[1], p(self.act), h_a,
+                                  M, H, I, h_b, ws, wsb, st))
+        last = h_a + (M - 1) * H * 4
+        chk(lib.qz_rmsnorm(last, p(self.norm_w), xn, 1, H, S.eps, st))
+        chk(lib.qz_gemv_w8(p(self.lm_q), p(self.lm_s), self.lm_s.shape[1], xn, p(self.logits),
+                           S.vocab, H, None, st))
+        self.pos_dev.fill_(pos0)
+        chk(lib.qz_argmax(p(self.logits), 1, S.vocab, p(self.keys), p(self.tok), p(self.pos_dev),
+                          M, st))
+        self.pos = pos0 + M
+        return int(self.tok.item())
+
+    def decode(self, token: int) -> int:
+        """One eager decode step from `token`; returns the greedy next token."""
+        if not 0 <= token < self.spec.vocab:
+            raise ValueError("token id outside the vocabulary")
+        if self.pos >= self.max_ctx:
+            raise ValueError("the cache is full")
+        self.tok.fill_(int(token))
+        self.pos_dev.fill_(self.pos)
+        self._decode_ops(self._stream())
+        self.pos += 1
+        return int(self.tok.item())
+
+    # ----------------------------------------------------------- graph replay
+    def capture(self, steps: int = 8) -> None:
+        """Capture `steps` consecutive decode steps (each followed by a copy of
+        its token into a device history slot) into one CUDA graph."""
+        steps = max(1, int(steps))
+        self._graph = None
+        self.hist = torch.zeros(steps, dtype=torch.int64, device=self.dev)
+        # One eager step first, so every launch path (kernel attributes, the
+        # cooperative-launch form) is settled outside the capture. It writes the
+        # cache row at the current position, which the next real step rewrites;
+        # token and device position are restored.
+        tok0 = self.tok.clone()
+        if self.pos < self.max_ctx:
+            self.pos_dev.fill_(self.pos)
+            self._decode_ops(self._stream())
+            self.tok.copy_(tok0)
+            self.pos_dev.fill_(self.pos)
+        side = torch.cuda.Stream(self.dev)
+        side.wait_stream(torch.cuda.current_stream(self.dev))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(g, stream=side):
+                st = side.cuda_stream
+                for i in range(steps):
+                    self._decode_ops(st)
+                    self.hist[i:i + 1].copy_(self.tok)
+        torch.cuda.current_stream(self.dev).wait_stream(side)
+        self._graph = g
+        self._graph_steps = steps
+
+    def replay(self) -> torch.Tensor:
+        """Run the captured steps from the current device token and position;
+        returns the device history of their tokens."""
+        if self._graph is None:
+            raise RuntimeError("capture() first")
+        if self.pos + self._graph_steps > self.max_ctx:
+            raise ValueError("the cache would overflow")
+        self._graph.replay()
+        self.pos += self._graph_steps
+        return self.hist
+
+    def generate(self, first: int, steps: int, *, graph: bool = True, unroll: int = 8
+                 ) -> list[int]:
+        """Greedy tokens after feeding `first` at the current position: the
+        decode loop of quartz/generate.py:52-58 (without EOS handling), `steps`
+        tokens, the first being the argmax of `first`'s logits."""
+        if steps <= 0:
+            return []
+        if self.pos + steps > self.max_ctx:
+            raise ValueError("generation would overflow the cache")
+        if not 0 <= first < self.spec.vocab:
+            raise ValueError("token id outside the vocabulary")
+        if not graph:
+            out, tok = [], first
+            for _ in range(steps):
+                tok = self.decode(tok)
+                out.append(tok)
+            return out
+        if self._graph is None or self._graph_steps != unroll:
+            self.capture(unroll)
+        out = torch.empty(steps, dtype=torch.int64, device=self.dev)
+        self.tok.fill_(int(first))
+        self.pos_dev.fill_(self.pos)
+        st = self._stream()
+        done = 0
+        while steps - done >= self._graph_steps:
+            h = self.replay()
+            out[done:done + self._graph_steps].copy_(h)
+            done += self._graph_steps
+        while done < steps:
+            self._decode_ops(st)
+            out[done:done + 1].copy_(self.tok)
+            self.pos += 1
+            done += 1
+        return out.cpu().tolist()

@@ -9,6 +9,15 @@ and streams.
     gemm(q, scale, X)            -> Y        quartz/kernels/int8.py:66-87
     fused_mlp(gu_q, gu_s, x, down_q, down_s)  -> out   quartz/kernels/fused.py:27-65
     silu_mul(gu)                 -> a        quartz/quantize.py:112-114 (+ ops.py:35-37)
+
+Decode-step glue (the fp32 work between the int8 matmuls of one token):
+
+    embed_gather(q, scale, ids)  -> rows     quartz/quantize.py:78-80
+    rmsnorm(x, w, eps)           -> y        quartz/ops.py:24-32
+    qk_rope(qkv, ...)            -> q        quartz/models/qwen3.py:31-41, rope.py:47-78
+    attention_decode(q, kc, vc, T)           quartz/attention.py:29-43 (one query row)
+    attention_prefill(q, kc, vc, pos0)       quartz/attention.py:15-43 (causal rows)
+    argmax(logits)               -> tokens   quartz/sample.py:21-22
 """
 
 from __future__ import annotations
@@ -233,3 +242,194 @@ def check_status(device=None) -> None:
         raise _lib.QuartzError(
             f"device kernels reported {count} failed wait(s): bits=0x{bits:x} "
             f"first site=0x{site:x} block={block}")
+
+
+# ---------------------------------------------------------------------------
+# decode-step glue
+# ---------------------------------------------------------------------------
+
+_attn_ws: dict[int, torch.Tensor] = {}
+_argmax_keys: dict[int, torch.Tensor] = {}
+
+
+def embed_gather(q, scale, ids, out=None):
+    """out[m, :] = q[ids[m], :] * scale[ids[m], group] (int64 ids on the device)."""
+    V, H, ng = _weights(q, scale)
+    ensure_device(q.device)
+    _need(ids, torch.int64, "ids")
+    M = ids.numel()
+    if out is None:
+        out = torch.empty((M, H), dtype=torch.float32, device=q.device)
+    _need(out, torch.float32, "out")
+    if out.numel() != M * H:
+        raise ValueError(f"out must hold M*H = {M * H} elements")
+    _same_device(q.device, scale, ids, out)
+    with torch.cuda.device(q.device):
+        _lib.check(_lib.load().qz_embed_gather(q.data_ptr(), scale.data_ptr(), ng, ids.data_ptr(),
+                                               M, V, H, out.data_ptr(), _stream_ptr(q.device)))
+    return out
+
+
+def rmsnorm(x, w, eps=1e-6, out=None):
+    """Row-wise x / sqrt(mean(x^2) + eps) * w over the last dimension."""
+    _need(x, torch.float32, "x")
+    _need(w, torch.float32, "w", 1)
+    ensure_device(x.device)
+    n = x.shape[-1]
+    if w.numel() != n:
+        raise ValueError(f"w has {w.numel()} elements, rows have {n}")
+    rows = x.numel() // n if n else 0
+    if out is None:
+        out = torch.empty_like(x)
+    _need(out, torch.float32, "out")
+    if out.numel() != x.numel():
+        raise ValueError("out must match x")
+    _same_device(x.device, w, out)
+    with torch.cuda.device(x.device):
+        _lib.check(_lib.load().qz_rmsnorm(x.data_ptr(), w.data_ptr(), out.data_ptr(), rows, n,
+                                          float(eps), _stream_ptr(x.device)))
+    return out
+
+
+def _cache_dims(kc, vc):
+    _need(kc, torch.float32, "k_cache", 3)
+    _need(vc, torch.float32, "v_cache", 3)
+    if kc.shape != vc.shape:
+        raise ValueError("k_cache and v_cache must have the same shape")
+    return kc.shape   # (n_kv, max_ctx, head_dim)
+
+
+def qk_rope(qkv, inv_freq, k_cache, v_cache, n_heads, pos0=0, pos_dev=None, q_norm=None,
+            k_norm=None, eps=1e-6, q_out=None):
+    """Split qkv [M, (nq + 2 nkv) hd] into q (normed, rotated; returned as [M, nq hd]) and the
+    cache rows at positions pos0 + m (or *pos_dev + m)."""
+    nkv, max_ctx, hd = _cache_dims(k_cache, v_cache)
+    _need(qkv, torch.float32, "qkv")
+    _need(inv_freq, torch.float32, "inv_freq", 1)
+    ensure_device(qkv.device)
+    width = (n_heads + 2 * nkv) * hd
+    if qkv.shape[-1] != width:
+        raise ValueError(f"qkv rows must have {width} elements")
+    if inv_freq.numel() != hd // 2:
+        raise ValueError("inv_freq must have head_dim / 2 elements")
+    M = qkv.numel() // width
+    for t, name in ((q_norm, "q_norm"), (k_norm, "k_norm")):
+        if t is not None:
+            _need(t, torch.float32, name, 1)
+            if t.numel() != hd:
+                raise ValueError(f"{name} must have head_dim elements")
+    if (q_norm is None) != (k_norm is None):
+        raise ValueError("pass both q_norm and k_norm or neither")
+    if pos_dev is not None:
+        _need(pos_dev, torch.int64, "pos_dev")
+    if q_out is None:
+        q_out = torch.empty((M, n_heads * hd), dtype=torch.float32, device=qkv.device)
+    _need(q_out, torch.float32, "q_out")
+    if q_out.numel() != M * n_heads * hd:
+        raise ValueError("q_out must hold M * n_heads * head_dim elements")
+    _same_device(qkv.device, inv_freq, k_cache, v_cache, q_norm, k_norm, pos_dev, q_out)
+    with torch.cuda.device(qkv.device):
+        _lib.check(_lib.load().qz_qk_rope(
+            qkv.data_ptr(), _ptr(q_norm), _ptr(k_norm), inv_freq.data_ptr(), q_out.data_ptr(),
+            k_cache.data_ptr(), v_cache.data_ptr(), M, n_heads, nkv, hd, max_ctx, int(pos0),
+            _ptr(pos_dev), float(eps), _stream_ptr(qkv.device)))
+    return q_out
+
+
+def attention_workspace(device, n_heads: int, head_dim: int, max_ctx: int) -> torch.Tensor:
+    """Grow-only per-device chunk-partials buffer of attention_decode."""
+    import ctypes
+    idx = ensure_device(device)
+    need = ctypes.c_int64(0)
+    _lib.check(_lib.load().qz_attention_decode_workspace_bytes(n_heads, head_dim, max_ctx,
+                                                               ctypes.byref(need)))
+    ws = _attn_ws.get(idx)
+    if ws is None or ws.numel() < need.value:
+        ws = torch.empty(need.value, dtype=torch.uint8, device=torch.device("cuda", idx))
+        _attn_ws[idx] = ws
+    return ws
+
+
+def attention_decode(q, k_cache, v_cache, T=None, T_dev=None, t_offset=0, scale=None, out=None,
+                     workspace=None):
+    """softmax(q K^T * scale) V for one query row per head over cache positions [0, T)
+    (T = *T_dev + t_offset when T_dev is given). q: [n_heads * head_dim]."""
+    nkv, max_ctx, hd = _cache_dims(k_cache, v_cache)
+    _need(q, torch.float32, "q")
+    ensure_device(q.device)
+    if q.numel() % hd:
+        raise ValueError("q must hold n_heads * head_dim elements")
+    nq = q.numel() // hd
+    if (T is None) == (T_dev is None):
+        raise ValueError("pass exactly one of T and T_dev")
+    if T_dev is not None:
+        _need(T_dev, torch.int64, "T_dev")
+    scale = hd ** -0.5 if scale is None else scale
+    if out is None:
+        out = torch.empty(nq * hd, dtype=torch.float32, device=q.device)
+    _need(out, torch.float32, "out")
+    if out.numel() != nq * hd:
+        raise ValueError("out must hold n_heads * head_dim elements")
+    ws = workspace if workspace is not None else attention_workspace(q.device, nq, hd, max_ctx)
+    _same_device(q.device, k_cache, v_cache, T_dev, out, ws)
+    with torch.cuda.device(q.device):
+        _lib.check(_lib.load().qz_attention_decode(
+            q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(), nq, nkv, hd,
+            max_ctx, 0 if T is None else int(T), _ptr(T_dev), int(t_offset), float(scale),
+            ws.data_ptr(), ws.numel(), _stream_ptr(q.device)))
+    return out
+
+
+def attention_prefill(q, k_cache, v_cache, pos0, scale=None, out=None):
+    """Causal attention of query rows q [M, n_heads * head_dim] at positions pos0 + m."""
+    nkv, max_ctx, hd = _cache_dims(k_cache, v_cache)
+    _need(q, torch.float32, "q", 2)
+    ensure_device(q.device)
+    M, width = q.shape
+    if width % hd:
+        raise ValueError("q rows must hold n_heads * head_dim elements")
+    nq = width // hd
+    scale = hd ** -0.5 if scale is None else scale
+    if out is None:
+        out = torch.empty_like(q)
+    _need(out, torch.float32, "out")
+    if out.numel() != q.numel():
+        raise ValueError("out must match q")
+    _same_device(q.device, k_cache, v_cache, out)
+    with torch.cuda.device(q.device):
+        _lib.check(_lib.load().qz_attention_prefill(
+            q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(), M, nq, nkv, hd,
+            max_ctx, int(pos0), float(scale), _stream_ptr(q.device)))
+    return out
+
+
+def argmax_keys(device, M: int) -> torch.Tensor:
+    """Per-device zeroed uint64 scratch for argmax (kept zero between calls)."""
+    idx = ensure_device(device)
+    keys = _argmax_keys.get(idx)
+    if keys is None or keys.numel() < M:
+        keys = torch.zeros(max(M, 64), dtype=torch.int64, device=torch.device("cuda", idx))
+        _argmax_keys[idx] = keys
+    return keys
+
+
+def argmax(logits, tokens=None, pos_dev=None, pos_step=0, keys=None):
+    """Greedy token per row of logits [M, V] (first index of the maximum)."""
+    _need(logits, torch.float32, "logits")
+    ensure_device(logits.device)
+    V = logits.shape[-1]
+    M = logits.numel() // V
+    if tokens is None:
+        tokens = torch.empty(M, dtype=torch.int64, device=logits.device)
+    _need(tokens, torch.int64, "tokens")
+    if tokens.numel() != M:
+        raise ValueError("tokens must have one element per row")
+    if pos_dev is not None:
+        _need(pos_dev, torch.int64, "pos_dev")
+    keys = keys if keys is not None else argmax_keys(logits.device, M)
+    _same_device(logits.device, tokens, pos_dev, keys)
+    with torch.cuda.device(logits.device):
+        _lib.check(_lib.load().qz_argmax(logits.data_ptr(), M, V, keys.data_ptr(),
+                                         tokens.data_ptr(), _ptr(pos_dev), int(pos_step),
+                                         _stream_ptr(logits.device)))
+    return tokens

@@ -1,0 +1,106 @@
+"""CPU checks of the decode workload's host side: the synthetic int8 checkpoint
+recipe reproduces quartz's own int8 tensors byte for byte (SHA-256 digests the
+reference recorded), the RoPE frequencies equal the reference's, and the model
+spec reads HF configs like quartz/config.py."""
+
+import hashlib
+import json
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from quartz_b200.model import (LLAMA_3P2_1B, QWEN3_0P6B, ModelSpec, leaf_names, norm_weights,
+                               random_int8_weights, rope_inv_freq, seeded_kv)
+
+HERE = Path(__file__).resolve().parent
+CASES = {c["id"]: c for c in json.loads((HERE / "golden" / "cases_model.json").read_text())["cases"]}
+
+
+def _golden(cid, key):
+    with np.load(HERE / "golden" / "golden_model.npz") as z:
+        return z[f"{cid}__{key}"]
+
+
+def _sha(a):
+    return hashlib.sha256(np.ascontiguousarray(a).tobytes()).hexdigest()
+
+
+def _spec(cid):
+    c = CASES[cid]
+    return ModelSpec.from_hf(c["cfg"], c["arch"])
+
+
+@pytest.mark.parametrize("cid", ["qwen3_tiny_prompt", "llama_tiny_prompt", "qwen3_tiny_kv"])
+def test_weight_digests_tiny(cid):
+    spec = _spec(cid)
+    w = {n: (q, s) for n, q, s in random_int8_weights(spec)}
+    d = CASES[cid]["digests"]
+    last = f"model.layers.{spec.layers - 1}.mlp.down_proj"
+    assert _sha(w["model.embed_tokens"][0]) == d["embed_q"]
+    assert _sha(w["model.embed_tokens"][1]) == d["embed_s"]
+    assert _sha(w["model.layers.0.self_attn.q_proj"][0]) == d["q_proj0"]
+    gu = np.concatenate([w["model.layers.0.mlp.gate_proj"][0], w["model.layers.0.mlp.up_proj"][0]])
+    assert _sha(gu) == d["gu_q0"]
+    assert _sha(w[last][0]) == d["down_last"]
+    if "lm_head_q" in d:
+        assert _sha(w["lm_head"][0]) == d["lm_head_q"]
+
+
+def test_weight_digests_qwen3_0p6b():
+    """The full Qwen3-0.6B draw (about 0.6 G values): embedding first, last layer's down."""
+    spec = _spec("qwen3_0p6b_kv512")
+    d = CASES["qwen3_0p6b_kv512"]["digests"]
+    last = f"model.layers.{spec.layers - 1}.mlp.down_proj"
+    for name, q, s in random_int8_weights(spec):
+        if name == "model.embed_tokens":
+            assert _sha(q) == d["embed_q"] and _sha(s) == d["embed_s"]
+        elif name == "model.layers.0.self_attn.q_proj":
+            assert _sha(q) == d["q_proj0"]
+        elif name == last:
+            assert _sha(q) == d["down_last"]
+
+
+@pytest.mark.parametrize("cid", sorted(CASES))
+def test_rope_inv_freq(cid):
+    try:
+        ref = _golden(cid, "inv_freq")
+    except KeyError:
+        pytest.skip("fixture predates the stored frequencies")
+    got = rope_inv_freq(_spec(cid))
+    assert got.dtype == np.float32 and np.array_equal(got, ref)
+
+
+def test_leaf_order_and_norms():
+    names = [n for n, _ in leaf_names(LLAMA_3P2_1B)]
+    assert names[0] == "model.embed_tokens" and names[-1].endswith("layers.15.mlp.down_proj")
+    assert names[1:8] == [f"model.layers.0.{p}" for p in
+                          ("self_attn.q_proj", "self_attn.k_proj", "self_attn.v_proj",
+                           "self_attn.o_proj", "mlp.gate_proj", "mlp.up_proj", "mlp.down_proj")]
+    untied = ModelSpec(**{**QWEN3_0P6B.__dict__, "tie": False})
+    assert leaf_names(untied)[-1] == ("lm_head", (151936, 1024))
+    n = norm_weights(QWEN3_0P6B)
+    assert len(n) == 1 + 4 * 28 and all((v == 1).all() for v in n.values())
+    assert not any("q_norm" in k for k in norm_weights(LLAMA_3P2_1B))
+
+
+def test_spec_from_hf_and_bytes():
+    s = ModelSpec.from_hf(dict(hidden_size=2048, num_hidden_layers=16, num_attention_heads=32,
+                               num_key_value_heads=8, intermediate_size=8192, vocab_size=128256,
+                               head_dim=None), "LlamaForCausalLM")
+    assert s.head_dim == 64 and not s.qk_norm and s.qkv_rows == 3072
+    # all-int8 Qwen3-0.6B streams about 0.6 GB of weights per token
+    assert 0.59e9 < QWEN3_0P6B.int8_bytes_per_token() < 0.60e9
+    with pytest.raises(ValueError):
+        ModelSpec(**{**QWEN3_0P6B.__dict__, "arch": "GPT2LMHeadModel"})
+
+
+def test_seeded_kv_shapes():
+    spec = _spec("qwen3_tiny_kv")
+    kv = list(seeded_kv(spec, 40))
+    assert len(kv) == spec.layers
+    k, v = kv[0]
+    assert k.shape == (spec.n_kv, 40, spec.head_dim) and k.dtype == np.float32
+    rng = np.random.default_rng(99)
+    k0 = rng.standard_normal((1, spec.n_kv, 40, spec.head_dim), dtype=np.float32)
+    assert np.array_equal(k, k0[0])
