@@ -170,18 +170,37 @@ int qz_qk_rope(const float* qkv, const float* q_norm_w, const float* k_norm_w,
                int nq, int nkv, int hd, int64_t max_ctx, int64_t pos0, const int64_t* pos_dev,
                float eps, void* stream);
 
-/* Workspace bytes qz_attention_decode needs for contexts up to max_ctx. */
-int qz_attention_decode_workspace_bytes(int nq, int hd, int64_t max_ctx, int64_t* bytes);
+/* Workspace bytes the decode attention entry points need for contexts up to
+ * max_ctx on the current device. The workspace must be 256-byte aligned and
+ * zeroed once before its first use (the kernels leave it ready for the next
+ * call); calls sharing one workspace must not overlap on the GPU. */
+int qz_attention_decode_workspace_bytes(int nq, int nkv, int hd, int64_t max_ctx, int64_t* bytes);
 
 /*
  * One query row per head over the first T cache positions:
  * out[h] = softmax(q[h] . K^T * scale) V, kv head h / (nq / nkv) (GQA by
  * repeat, quartz/attention.py:29-43). T_dev, if not NULL, replaces T with
- * *T_dev + t_offset (for graph replay).
+ * *T_dev + t_offset (for graph replay). The context is split across CTAs and
+ * the last CTA of each kv head merges the partial softmaxes.
  */
 int qz_attention_decode(const float* q, const float* k_cache, const float* v_cache, float* out,
                         int nq, int nkv, int hd, int64_t max_ctx, int64_t T, const int64_t* T_dev,
                         int64_t t_offset, float scale, void* ws, size_t ws_bytes, void* stream);
+
+/*
+ * The whole attention block of one decode token after the q/k/v projections,
+ * in one launch: from the projection row qkv [(nq + 2 nkv) hd] (q heads, k
+ * heads, v heads), optional per-head q/k RMSNorm (Qwen3,
+ * quartz/models/qwen3.py:33-34; NULL weights for Llama), RoPE at position
+ * pos (quartz/rope.py:47-78), append of k/v at pos (quartz/cache.py:26-46),
+ * then qz_attention_decode over positions [0, pos]. pos = *pos_dev when
+ * pos_dev is not NULL (graph replay), else pos0.
+ */
+int qz_attention_decode_qkv(const float* qkv, const float* q_norm_w, const float* k_norm_w,
+                            const float* inv_freq, float* k_cache, float* v_cache, float* out,
+                            int nq, int nkv, int hd, int64_t max_ctx, int64_t pos0,
+                            const int64_t* pos_dev, float eps, float scale, void* ws,
+                            size_t ws_bytes, void* stream);
 
 /* M query rows at positions pos0 .. pos0 + M - 1, each attending causally to
  * cache positions 0 .. its own (the additive mask of quartz/attention.py:15-26). */

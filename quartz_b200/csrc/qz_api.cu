@@ -618,10 +618,89 @@ int qz_qk_rope(const float* qkv, const float* q_norm_w, const float* k_norm_w,
   return QZ_OK;
 }
 
-int qz_attention_decode_workspace_bytes(int nq, int hd, int64_t max_ctx, int64_t* bytes) {
-  if (!bytes || nq < 1 || hd < 1 || max_ctx < 1)
+}  // extern "C"
+
+namespace {
+
+// Decode-attention workspace: [tickets: n_kv u32, padded to 256 B]
+// [fused partials: n_kv * S * n_rep * (hd + 2) fp32, or the chunked kernels'
+// nq * ceil(max_ctx / 64) * (hd + 2), whichever is larger] [q scratch: nq * hd fp32].
+struct AttnLayout {
+  int S;
+  int64_t part_off, q_off, total;
+};
+
+int attn_splits(const DeviceInfo& d, int nkv, int64_t max_ctx) {
+  const int64_t s = std::min<int64_t>(qz::cdiv(d.sms, nkv), qz::cdiv(max_ctx, 32));
+  return static_cast<int>(std::max<int64_t>(1, s));
+}
+
+AttnLayout attn_layout(const DeviceInfo& d, int nq, int nkv, int hd, int64_t max_ctx) {
+  AttnLayout l;
+  l.S = attn_splits(d, nkv, max_ctx);
+  auto al = [](int64_t b) { return ((b + 255) / 256) * 256; };
+  const int64_t fused = static_cast<int64_t>(nkv) * l.S * (nq / nkv) * (hd + 2) * 4;
+  const int64_t chunked = static_cast<int64_t>(nq) * qz::cdiv(max_ctx, qz::dec::kChunk) * (hd + 2) * 4;
+  l.part_off = al(static_cast<int64_t>(nkv) * 4);
+  l.q_off = l.part_off + al(std::max(fused, chunked));
+  l.total = l.q_off + al(static_cast<int64_t>(nq) * hd * 4);
+  return l;
+}
+
+template <int E, int NR, bool QKV>
+int launch_attn_fused(const qz::dec::AttnArgs& a, int S, cudaStream_t st) {
+  constexpr int smem = qz::dec::attn_fused_smem<E, NR>();
+  static_assert(smem <= 48 * 1024, "fused attention shared memory above the default limit");
+  qz::dec::attn_decode_fused_kernel<E, NR, QKV>
+      <<<dim3(static_cast<unsigned>(a.nkv), static_cast<unsigned>(S)), qz::dec::kAttnThreads,
+         smem, st>>>(a);
+  QZ_CUDA(cudaGetLastError());
+  return QZ_OK;
+}
+
+template <bool QKV>
+int dispatch_attn_fused(int hd, int n_rep, const qz::dec::AttnArgs& a, int S, cudaStream_t st,
+                        bool* done) {
+  *done = true;
+#define QZ_ATTN_CASE(E_, NR_) \
+  if (hd == 32 * (E_) && n_rep == (NR_)) return launch_attn_fused<E_, NR_, QKV>(a, S, st);
+  QZ_ATTN_CASE(2, 1) QZ_ATTN_CASE(2, 2) QZ_ATTN_CASE(2, 4) QZ_ATTN_CASE(2, 8)
+  QZ_ATTN_CASE(4, 1) QZ_ATTN_CASE(4, 2) QZ_ATTN_CASE(4, 4) QZ_ATTN_CASE(4, 8)
+  QZ_ATTN_CASE(8, 1) QZ_ATTN_CASE(8, 2) QZ_ATTN_CASE(8, 4)
+#undef QZ_ATTN_CASE
+  *done = false;
+  return QZ_OK;
+}
+
+bool aligned_to(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// The chunked kernels (any head_dim <= 256, n_rep <= 8): attention + combine.
+int attn_chunked(const float* q, const float* kc, const float* vc, float* out, int nq, int nkv,
+                 int hd, int64_t max_ctx, int64_t T, const int64_t* T_dev, int64_t t_offset,
+                 float scale, float* part, cudaStream_t st) {
+  const int64_t span = T_dev ? max_ctx : T;
+  const int64_t nchunks = qz::cdiv(span, qz::dec::kChunk);
+  const int n_rep = nq / nkv;
+  const int smem = (n_rep * hd + n_rep * qz::dec::kChunk) * 4;
+  const dim3 grid(static_cast<unsigned>(nkv), static_cast<unsigned>(nchunks));
+  qz::dec::attn_decode_kernel<<<grid, 256, smem, st>>>(q, kc, vc, part, nq, nkv, hd, max_ctx, T,
+                                                       T_dev, t_offset, scale);
+  QZ_CUDA(cudaGetLastError());
+  qz::dec::attn_combine_kernel<<<static_cast<unsigned>(nq), 128, 0, st>>>(
+      part, out, hd, static_cast<int>(nchunks));
+  QZ_CUDA(cudaGetLastError());
+  return QZ_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int qz_attention_decode_workspace_bytes(int nq, int nkv, int hd, int64_t max_ctx, int64_t* bytes) {
+  if (!bytes || nq < 1 || nkv < 1 || nq % nkv || hd < 1 || max_ctx < 1)
     return fail(QZ_ERR_INVALID, "qz_attention_decode_workspace_bytes: bad arguments");
-  *bytes = static_cast<int64_t>(nq) * qz::cdiv(max_ctx, qz::dec::kChunk) * (hd + 2) * 4;
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  *bytes = attn_layout(*d, nq, nkv, hd, max_ctx).total;
   return QZ_OK;
 }
 
@@ -634,24 +713,91 @@ int qz_attention_decode(const float* q, const float* k_cache, const float* v_cac
     return fail(QZ_ERR_INVALID, "qz_attention_decode: context length outside [1, max_ctx]");
   if (!q || !k_cache || !v_cache || !out || !ws)
     return fail(QZ_ERR_INVALID, "qz_attention_decode: null pointer");
-  // With the length in device memory every chunk of the cache gets a block.
-  const int64_t span = T_dev ? max_ctx : T;
-  const int64_t nchunks = qz::cdiv(span, qz::dec::kChunk);
-  const int64_t need = static_cast<int64_t>(nq) * nchunks * (hd + 2) * 4;
-  if (static_cast<int64_t>(ws_bytes) < need)
-    return fail(QZ_ERR_INVALID, "qz_attention_decode: workspace too small");
-  float* part = static_cast<float*>(ws);
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  const AttnLayout L = attn_layout(*d, nq, nkv, hd, max_ctx);
+  if (static_cast<int64_t>(ws_bytes) < L.total || !aligned_to(ws, 256))
+    return fail(QZ_ERR_INVALID, "qz_attention_decode: workspace too small or not 256-byte aligned");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int n_rep = nq / nkv;
-  const int smem = (n_rep * hd + n_rep * qz::dec::kChunk) * 4;
-  const dim3 grid(static_cast<unsigned>(nkv), static_cast<unsigned>(nchunks));
-  qz::dec::attn_decode_kernel<<<grid, 256, smem, st>>>(q, k_cache, v_cache, part, nq, nkv, hd,
-                                                       max_ctx, T, T_dev, t_offset, scale);
+  char* w = static_cast<char*>(ws);
+  float* part = reinterpret_cast<float*>(w + L.part_off);
+  if (aligned16(q) && aligned16(k_cache) && aligned16(v_cache)) {
+    qz::dec::AttnArgs a{};
+    a.in = q;
+    a.kc = const_cast<float*>(k_cache);
+    a.vc = const_cast<float*>(v_cache);
+    a.out = out;
+    a.part = part;
+    a.tickets = reinterpret_cast<unsigned*>(w);
+    a.len_dev = T_dev;
+    a.len0 = T_dev ? 0 : T;
+    a.len_off = T_dev ? t_offset : 0;
+    a.max_ctx = max_ctx;
+    a.nq = nq;
+    a.nkv = nkv;
+    a.scale = scale;
+    bool done = false;
+    if (int rc = dispatch_attn_fused<false>(hd, nq / nkv, a, L.S, st, &done)) return rc;
+    if (done) return QZ_OK;
+  }
+  return attn_chunked(q, k_cache, v_cache, out, nq, nkv, hd, max_ctx, T, T_dev, t_offset, scale,
+                      part, st);
+}
+
+int qz_attention_decode_qkv(const float* qkv, const float* q_norm_w, const float* k_norm_w,
+                            const float* inv_freq, float* k_cache, float* v_cache, float* out,
+                            int nq, int nkv, int hd, int64_t max_ctx, int64_t pos0,
+                            const int64_t* pos_dev, float eps, float scale, void* ws,
+                            size_t ws_bytes, void* stream) {
+  if (int rc = check_heads(nq, nkv, hd, "qz_attention_decode_qkv")) return rc;
+  if (max_ctx < 1) return fail(QZ_ERR_INVALID, "qz_attention_decode_qkv: bad max_ctx");
+  if (!pos_dev && (pos0 < 0 || pos0 >= max_ctx))
+    return fail(QZ_ERR_INVALID, "qz_attention_decode_qkv: position outside the cache");
+  if (!qkv || !inv_freq || !k_cache || !v_cache || !out || !ws)
+    return fail(QZ_ERR_INVALID, "qz_attention_decode_qkv: null pointer");
+  if ((q_norm_w == nullptr) != (k_norm_w == nullptr))
+    return fail(QZ_ERR_INVALID, "qz_attention_decode_qkv: pass both norm weights or neither");
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  const AttnLayout L = attn_layout(*d, nq, nkv, hd, max_ctx);
+  if (static_cast<int64_t>(ws_bytes) < L.total || !aligned_to(ws, 256))
+    return fail(QZ_ERR_INVALID,
+                "qz_attention_decode_qkv: workspace too small or not 256-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  char* w = static_cast<char*>(ws);
+  float* part = reinterpret_cast<float*>(w + L.part_off);
+  if (aligned16(qkv) && aligned16(k_cache) && aligned16(v_cache)) {
+    qz::dec::AttnArgs a{};
+    a.in = qkv;
+    a.qn_w = q_norm_w;
+    a.kn_w = k_norm_w;
+    a.inv_freq = inv_freq;
+    a.kc = k_cache;
+    a.vc = v_cache;
+    a.out = out;
+    a.part = part;
+    a.tickets = reinterpret_cast<unsigned*>(w);
+    a.len_dev = pos_dev;
+    a.len0 = pos_dev ? 0 : pos0;
+    a.len_off = 1;
+    a.max_ctx = max_ctx;
+    a.nq = nq;
+    a.nkv = nkv;
+    a.scale = scale;
+    a.eps = eps;
+    bool done = false;
+    if (int rc = dispatch_attn_fused<true>(hd, nq / nkv, a, L.S, st, &done)) return rc;
+    if (done) return QZ_OK;
+  }
+  // other shapes: rope + append, then the chunked kernels
+  float* qs = reinterpret_cast<float*>(w + L.q_off);
+  const dim3 grid(1u, static_cast<unsigned>(nq + 2 * nkv));
+  qz::dec::qk_rope_kernel<<<grid, 128, hd * sizeof(float), st>>>(
+      qkv, q_norm_w, k_norm_w, inv_freq, qs, k_cache, v_cache, nq, nkv, hd, max_ctx, pos0, pos_dev,
+      eps);
   QZ_CUDA(cudaGetLastError());
-  qz::dec::attn_combine_kernel<<<static_cast<unsigned>(nq), 128, 0, st>>>(
-      part, out, hd, static_cast<int>(nchunks));
-  QZ_CUDA(cudaGetLastError());
-  return QZ_OK;
+  return attn_chunked(qs, k_cache, v_cache, out, nq, nkv, hd, max_ctx, pos_dev ? 0 : pos0 + 1,
+                      pos_dev, 1, scale, part, st);
 }
 
 int qz_attention_prefill(const float* q, const float* k_cache, const float* v_cache, float* out,

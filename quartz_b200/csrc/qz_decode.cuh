@@ -261,6 +261,280 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(
   }
 }
 
+// ---------------------------------------------------------------------------
+// Fused decode attention, one query row: split-context (flash-decoding) with
+// the q/k preparation and the KV append folded in and the cross-CTA merge done
+// by the last CTA to finish (an atomic ticket per kv head; nothing waits).
+//
+// Grid (n_kv, S). CTA (g, c) owns the kv head g, its NR = nq / nkv query heads
+// g*NR .. g*NR + NR - 1 (quartz repeats each kv head to NR adjacent query
+// heads, quartz/attention.py:36-38), and the cache positions
+// [c * per, min(T, (c + 1) * per)), per = ceil(T / S) rounded up to 8. The
+// context length T is read on the device, so one captured launch serves every
+// position.
+//
+// With QKV the input is the raw projection row [(nq + 2 nkv) hd]: every CTA
+// normalises (Qwen3's per-head RMSNorm, quartz/models/qwen3.py:33-34) and
+// rotates (half-split RoPE, quartz/rope.py:47-78) its query heads; the CTA
+// owning position T - 1 also prepares that position's key and value and
+// appends them to the cache before reading it (quartz/cache.py:26-46).
+// Without QKV the input is q [nq hd], already rotated, and the cache is read only.
+//
+// Lane l of a warp holds head elements [l E, l E + E) (hd = 32 E), so the
+// RoPE partner of element i < hd/2, element i + hd/2, is in lane l ^ 16.
+// Each warp runs an online softmax over every 8th position of the CTA's range,
+// U positions per round; the 8 warps merge in shared memory into one partial
+// (acc[hd], max, sum) per query head, written to the workspace.
+// ---------------------------------------------------------------------------
+struct AttnArgs {
+  const float* in;        // QKV: qkv row [(nq + 2 nkv) hd]; else q [nq hd]
+  const float* qn_w;      // [hd] or null
+  const float* kn_w;      // [hd] or null
+  const float* inv_freq;  // [hd / 2]
+  float* kc;              // [nkv, max_ctx, hd] (written only with QKV)
+  float* vc;
+  float* out;             // [nq hd]
+  float* part;            // [nkv][S][NR][hd + 2]
+  unsigned* tickets;      // [nkv], zero between launches
+  const int64_t* len_dev; // T = (len_dev ? *len_dev : len0) + len_off
+  int64_t len0, len_off, max_ctx;
+  int nq, nkv;
+  float scale, eps;
+};
+
+constexpr int kAttnThreads = 256;
+constexpr int kAttnWarps = kAttnThreads / 32;
+
+template <int E>
+__device__ __forceinline__ void load_vec(const float* p, float (&x)[E]) {
+  if constexpr (E == 4) {
+    const float4 v = *reinterpret_cast<const float4*>(p);
+    x[0] = v.x; x[1] = v.y; x[2] = v.z; x[3] = v.w;
+  } else if constexpr (E == 2) {
+    const float2 v = *reinterpret_cast<const float2*>(p);
+    x[0] = v.x; x[1] = v.y;
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; e += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(p + e);
+      x[e] = v.x; x[e + 1] = v.y; x[e + 2] = v.z; x[e + 3] = v.w;
+    }
+  }
+}
+
+template <int E>
+__device__ __forceinline__ void store_vec(float* p, const float (&x)[E]) {
+  if constexpr (E == 4) {
+    *reinterpret_cast<float4*>(p) = make_float4(x[0], x[1], x[2], x[3]);
+  } else if constexpr (E == 2) {
+    *reinterpret_cast<float2*>(p) = make_float2(x[0], x[1]);
+  } else {
+#pragma unroll
+    for (int e = 0; e < E; e += 4)
+      *reinterpret_cast<float4*>(p + e) = make_float4(x[e], x[e + 1], x[e + 2], x[e + 3]);
+  }
+}
+
+// Optional per-head RMSNorm, then half-split RoPE at position pos, of the
+// head slice x held E elements per lane (whole warp participates).
+template <int E>
+__device__ __forceinline__ void norm_rope(float (&x)[E], const float* __restrict__ w,
+                                          const float* __restrict__ inv_freq, int64_t pos,
+                                          float eps, int lane) {
+  constexpr int HD = 32 * E, D = HD / 2;
+  if (w) {
+    float ss = 0.f;
+#pragma unroll
+    for (int e = 0; e < E; ++e) ss = fmaf(x[e], x[e], ss);
+    ss = warp_sum_f(ss);
+    const float r = 1.0f / sqrtf(ss / static_cast<float>(HD) + eps);
+#pragma unroll
+    for (int e = 0; e < E; ++e) x[e] = x[e] * r * w[lane * E + e];
+  }
+  const float fpos = static_cast<float>(pos);
+  const bool lower = lane < 16;
+#pragma unroll
+  for (int e = 0; e < E; ++e) {
+    const float other = __shfl_xor_sync(0xffffffffu, x[e], 16);
+    const int j = lane * E + e - (lower ? 0 : D);
+    const float ang = fpos * inv_freq[j];
+    const float c = cosf(ang), s = sinf(ang);
+    // lower: x1 c - x2 s (self x1, partner x2); upper: x2 c + x1 s (self x2, partner x1)
+    x[e] = lower ? x[e] * c - other * s : x[e] * c + other * s;
+  }
+}
+
+template <int E, int NR, bool QKV>
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_fused_kernel(AttnArgs a) {
+  constexpr int HD = 32 * E;
+  constexpr int U = E >= 8 ? 2 : 4;   // positions per warp per round
+  extern __shared__ float4 attn_smem4[];
+  float* qs = reinterpret_cast<float*>(attn_smem4);   // [NR][HD]
+  float* red = qs + NR * HD;                           // [warps][NR][HD + 2]
+  __shared__ unsigned s_last;
+  const int g = blockIdx.x, c = blockIdx.y, S = gridDim.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int64_t T = (a.len_dev ? *a.len_dev : a.len0) + a.len_off;
+  T = T > a.max_ctx ? a.max_ctx : T;
+  const int64_t per = T > 0 ? (cdiv(T, S) + 7) / 8 * 8 : 0;
+  const int64_t t0 = static_cast<int64_t>(c) * per;
+  const int64_t t1 = min64(T, t0 + per);
+  const int64_t pos = T - 1;
+  // the append happens only for a position inside the cache
+  const int64_t t_raw = (a.len_dev ? *a.len_dev : a.len0) + a.len_off;
+  const bool append = QKV && t_raw >= 1 && t_raw <= a.max_ctx;
+  float* pbase = a.part + (static_cast<int64_t>(g) * S + c) * NR * (HD + 2);
+  const int64_t kv_off = static_cast<int64_t>(g) * a.max_ctx * HD;
+
+  if (t0 < t1) {
+    // queries of this group (and, in the owning CTA, the new key/value)
+    for (int r = warp; r < NR; r += kAttnWarps) {
+      float x[E];
+      load_vec<E>(a.in + static_cast<int64_t>(g * NR + r) * HD + lane * E, x);
+      if constexpr (QKV) norm_rope<E>(x, a.qn_w, a.inv_freq, pos, a.eps, lane);
+#pragma unroll
+      for (int e = 0; e < E; ++e) qs[r * HD + lane * E + e] = x[e];
+    }
+    if constexpr (QKV) {
+      if (append && t0 <= pos && pos < t1 && warp == NR % kAttnWarps) {
+        float k[E], v[E];
+        load_vec<E>(a.in + static_cast<int64_t>(a.nq + g) * HD + lane * E, k);
+        load_vec<E>(a.in + static_cast<int64_t>(a.nq + a.nkv + g) * HD + lane * E, v);
+        norm_rope<E>(k, a.kn_w, a.inv_freq, pos, a.eps, lane);
+        store_vec<E>(a.kc + kv_off + pos * HD + lane * E, k);
+        store_vec<E>(a.vc + kv_off + pos * HD + lane * E, v);
+      }
+    }
+    __syncthreads();   // queries in shared memory; the appended row visible to the CTA
+
+    float q[NR][E], acc[NR][E], m[NR], l[NR];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+      m[r] = -INFINITY;
+      l[r] = 0.f;
+#pragma unroll
+      for (int e = 0; e < E; ++e) {
+        q[r][e] = qs[r * HD + lane * E + e];
+        acc[r][e] = 0.f;
+      }
+    }
+    for (int64_t tb = t0 + warp; tb < t1; tb += kAttnWarps * U) {
+      float kr[U][E], vr[U][E];
+      bool ok[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t t = tb + u * kAttnWarps;
+        ok[u] = t < t1;
+        if (ok[u]) {
+          load_vec<E>(a.kc + kv_off + t * HD + lane * E, kr[u]);
+          load_vec<E>(a.vc + kv_off + t * HD + lane * E, vr[u]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < E; ++e) kr[u][e] = vr[u][e] = 0.f;
+        }
+      }
+      float sc[U][NR];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int r = 0; r < NR; ++r) {
+          float d = 0.f;
+#pragma unroll
+          for (int e = 0; e < E; ++e) d = fmaf(q[r][e], kr[u][e], d);
+          sc[u][r] = d;
+        }
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+#pragma unroll
+        for (int r = 0; r < NR; ++r) sc[u][r] = warp_sum_f(sc[u][r]) * a.scale;
+#pragma unroll
+      for (int r = 0; r < NR; ++r) {
+        float mx = m[r];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (ok[u]) mx = fmaxf(mx, sc[u][r]);
+        const float corr = expf(m[r] - mx);
+        l[r] *= corr;
+#pragma unroll
+        for (int e = 0; e < E; ++e) acc[r][e] *= corr;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          if (!ok[u]) continue;
+          const float p = expf(sc[u][r] - mx);
+          l[r] += p;
+#pragma unroll
+          for (int e = 0; e < E; ++e) acc[r][e] = fmaf(p, vr[u][e], acc[r][e]);
+        }
+        m[r] = mx;
+      }
+    }
+    // merge the warps: per-warp (acc, m, l) to shared memory, then one partial per head
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+      float* wr = red + (warp * NR + r) * (HD + 2);
+#pragma unroll
+      for (int e = 0; e < E; ++e) wr[lane * E + e] = acc[r][e];
+      if (lane == 0) { wr[HD] = m[r]; wr[HD + 1] = l[r]; }
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < NR * HD; i += kAttnThreads) {
+      const int r = i / HD, d = i - r * HD;
+      float M = -INFINITY;
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; ++w) M = fmaxf(M, red[(w * NR + r) * (HD + 2) + HD]);
+      float num = 0.f, den = 0.f;
+#pragma unroll
+      for (int w = 0; w < kAttnWarps; ++w) {
+        const float* wr = red + (w * NR + r) * (HD + 2);
+        if (wr[HD] == -INFINITY) continue;
+        const float f = expf(wr[HD] - M);
+        num = fmaf(f, wr[d], num);
+        den = fmaf(f, wr[HD + 1], den);
+      }
+      pbase[r * (HD + 2) + d] = num;
+      if (d == 0) { pbase[r * (HD + 2) + HD] = M; pbase[r * (HD + 2) + HD + 1] = den; }
+    }
+  } else {
+    for (int r = threadIdx.x; r < NR; r += kAttnThreads) {
+      pbase[r * (HD + 2) + HD] = -INFINITY;
+      pbase[r * (HD + 2) + HD + 1] = 0.f;
+    }
+  }
+
+  // the last CTA of kv head g merges the S partials of its query heads
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    s_last = atomicAdd(a.tickets + g, 1u) == static_cast<unsigned>(S - 1);
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const float* gbase = a.part + static_cast<int64_t>(g) * S * NR * (HD + 2);
+  for (int i = threadIdx.x; i < NR * HD; i += kAttnThreads) {
+    const int r = i / HD, d = i - r * HD;
+    float M = -INFINITY, num = 0.f, den = 0.f;
+    for (int cc = 0; cc < S; ++cc) {
+      const float* pr = gbase + (cc * NR + r) * (HD + 2);
+      const float mc = __ldcg(pr + HD);
+      if (mc == -INFINITY) continue;
+      const float lc = __ldcg(pr + HD + 1), ac = __ldcg(pr + d);
+      const float Mn = fmaxf(M, mc);
+      const float fo = expf(M - Mn), fn = expf(mc - Mn);
+      num = num * fo + ac * fn;
+      den = den * fo + lc * fn;
+      M = Mn;
+    }
+    a.out[static_cast<int64_t>(g * NR + r) * HD + d] = num / den;
+  }
+  if (threadIdx.x == 0) a.tickets[g] = 0u;
+}
+
+template <int E, int NR>
+constexpr int attn_fused_smem() {
+  return (NR * 32 * E + kAttnWarps * NR * (32 * E + 2)) * 4;
+}
+
 // Greedy argmax of each row of logits [M, V]: a block reduces a slice of a row
 // to one packed key (order-preserving float bits << 32 | ~index) and
 // atomicMax-es it into keys[m] (zeroed before); larger value wins, then the

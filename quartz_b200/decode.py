@@ -149,9 +149,10 @@ class DecodeEngine:
         self.mlp_ws = torch.zeros(self.lib.qz_mlp_workspace_bytes() // 4, dtype=torch.int32,
                                   device=dev)
         b = ctypes.c_int64(0)
-        _lib.check(self.lib.qz_attention_decode_workspace_bytes(S.n_heads, hd, self.max_ctx,
-                                                                ctypes.byref(b)))
-        self.attn_ws = torch.empty(b.value, dtype=torch.uint8, device=dev)
+        with torch.cuda.device(dev):
+            _lib.check(self.lib.qz_attention_decode_workspace_bytes(
+                S.n_heads, S.n_kv, hd, self.max_ctx, ctypes.byref(b)))
+        self.attn_ws = torch.zeros(b.value, dtype=torch.uint8, device=dev)
         self.gemm_ws = None
         if Mx > 1:
             need = 0
@@ -212,12 +213,11 @@ class DecodeEngine:
             chk(lib.qz_rmsnorm(h_a, p(L.in_w), xn, 1, H, S.eps, st))
             chk(lib.qz_gemv_w8(p(L.qkv_q), p(L.qkv_s), L.qkv_s.shape[1], xn, p(self.qkv),
                                S.qkv_rows, H, None, st))
-            chk(lib.qz_qk_rope(p(self.qkv), qd._ptr(L.qn_w), qd._ptr(L.kn_w), p(self.inv_freq),
-                               p(self.qo), kc, vc, 1, nq, nkv, hd, self.max_ctx, 0,
-                               p(self.pos_dev), S.eps, st))
-            chk(lib.qz_attention_decode(p(self.qo), kc, vc, p(self.ao), nq, nkv, hd, self.max_ctx,
-                                        0, p(self.pos_dev), 1, self.attn_scale, p(self.attn_ws),
-                                        self.attn_ws.numel(), st))
+            chk(lib.qz_attention_decode_qkv(p(self.qkv), qd._ptr(L.qn_w), qd._ptr(L.kn_w),
+                                            p(self.inv_freq), kc, vc, p(self.ao), nq, nkv, hd,
+                                            self.max_ctx, 0, p(self.pos_dev), S.eps,
+                                            self.attn_scale, p(self.attn_ws),
+                                            self.attn_ws.numel(), st))
             chk(lib.qz_gemv_w8(p(L.o_q), p(L.o_s), L.o_s.shape[1], p(self.ao), h_b, H, nq * hd,
                                h_a, st))
             chk(lib.qz_rmsnorm(h_b, p(L.post_w), xn, 1, H, S.eps, st))
@@ -231,8 +231,9 @@ class DecodeEngine:
                           1, st))
 
     def _launches_per_token(self) -> int:
-        # embed + per layer (rmsnorm, qkv, rope, attn x2, o, rmsnorm, mlp) + norm, lm, argmax x2
-        return 1 + 8 * self.spec.layers + 4
+        # embed + per layer (rmsnorm, qkv, attention, o, rmsnorm, mlp) + norm, lm, argmax x2;
+        # attention is one launch for the head shapes of the fused kernel
+        return 1 + 6 * self.spec.layers + 4
 
     def prefill(self, ids: Iterable[int]) -> int:
         """Run the prompt ids at the current position; return the greedy next token

@@ -16,6 +16,7 @@ Decode-step glue (the fp32 work between the int8 matmuls of one token):
     rmsnorm(x, w, eps)           -> y        quartz/ops.py:24-32
     qk_rope(qkv, ...)            -> q        quartz/models/qwen3.py:31-41, rope.py:47-78
     attention_decode(q, kc, vc, T)           quartz/attention.py:29-43 (one query row)
+    attention_decode_qkv(qkv, ...)           the two above plus the KV append, one launch
     attention_prefill(q, kc, vc, pos0)       quartz/attention.py:15-43 (causal rows)
     argmax(logits)               -> tokens   quartz/sample.py:21-22
 """
@@ -336,16 +337,19 @@ def qk_rope(qkv, inv_freq, k_cache, v_cache, n_heads, pos0=0, pos_dev=None, q_no
     return q_out
 
 
-def attention_workspace(device, n_heads: int, head_dim: int, max_ctx: int) -> torch.Tensor:
-    """Grow-only per-device chunk-partials buffer of attention_decode."""
+def attention_workspace(device, n_heads: int, n_kv: int, head_dim: int, max_ctx: int
+                        ) -> torch.Tensor:
+    """Grow-only per-device workspace of the decode attention (zeroed when made;
+    the kernels leave it zeroed where it must be)."""
     import ctypes
     idx = ensure_device(device)
     need = ctypes.c_int64(0)
-    _lib.check(_lib.load().qz_attention_decode_workspace_bytes(n_heads, head_dim, max_ctx,
-                                                               ctypes.byref(need)))
+    with torch.cuda.device(idx):
+        _lib.check(_lib.load().qz_attention_decode_workspace_bytes(n_heads, n_kv, head_dim,
+                                                                   max_ctx, ctypes.byref(need)))
     ws = _attn_ws.get(idx)
     if ws is None or ws.numel() < need.value:
-        ws = torch.empty(need.value, dtype=torch.uint8, device=torch.device("cuda", idx))
+        ws = torch.zeros(need.value, dtype=torch.uint8, device=torch.device("cuda", idx))
         _attn_ws[idx] = ws
     return ws
 
@@ -370,13 +374,55 @@ def attention_decode(q, k_cache, v_cache, T=None, T_dev=None, t_offset=0, scale=
     _need(out, torch.float32, "out")
     if out.numel() != nq * hd:
         raise ValueError("out must hold n_heads * head_dim elements")
-    ws = workspace if workspace is not None else attention_workspace(q.device, nq, hd, max_ctx)
+    ws = workspace if workspace is not None else attention_workspace(q.device, nq, nkv, hd,
+                                                                      max_ctx)
     _same_device(q.device, k_cache, v_cache, T_dev, out, ws)
     with torch.cuda.device(q.device):
         _lib.check(_lib.load().qz_attention_decode(
             q.data_ptr(), k_cache.data_ptr(), v_cache.data_ptr(), out.data_ptr(), nq, nkv, hd,
             max_ctx, 0 if T is None else int(T), _ptr(T_dev), int(t_offset), float(scale),
             ws.data_ptr(), ws.numel(), _stream_ptr(q.device)))
+    return out
+
+
+def attention_decode_qkv(qkv, inv_freq, k_cache, v_cache, n_heads, pos0=0, pos_dev=None,
+                         q_norm=None, k_norm=None, eps=1e-6, scale=None, out=None,
+                         workspace=None):
+    """The attention block of one decode token from its projection row qkv
+    [(nq + 2 nkv) hd]: q/k norm (Qwen3), RoPE, k/v append at position pos0
+    (or *pos_dev), attention over positions [0, pos]. Returns [nq * hd]."""
+    nkv, max_ctx, hd = _cache_dims(k_cache, v_cache)
+    _need(qkv, torch.float32, "qkv")
+    _need(inv_freq, torch.float32, "inv_freq", 1)
+    ensure_device(qkv.device)
+    if qkv.numel() != (n_heads + 2 * nkv) * hd:
+        raise ValueError(f"qkv must hold (n_heads + 2 n_kv) * head_dim elements")
+    if inv_freq.numel() != hd // 2:
+        raise ValueError("inv_freq must have head_dim / 2 elements")
+    if (q_norm is None) != (k_norm is None):
+        raise ValueError("pass both q_norm and k_norm or neither")
+    for t, name in ((q_norm, "q_norm"), (k_norm, "k_norm")):
+        if t is not None:
+            _need(t, torch.float32, name, 1)
+            if t.numel() != hd:
+                raise ValueError(f"{name} must have head_dim elements")
+    if pos_dev is not None:
+        _need(pos_dev, torch.int64, "pos_dev")
+    scale = hd ** -0.5 if scale is None else scale
+    if out is None:
+        out = torch.empty(n_heads * hd, dtype=torch.float32, device=qkv.device)
+    _need(out, torch.float32, "out")
+    if out.numel() != n_heads * hd:
+        raise ValueError("out must hold n_heads * head_dim elements")
+    ws = workspace if workspace is not None else attention_workspace(qkv.device, n_heads, nkv, hd,
+                                                                      max_ctx)
+    _same_device(qkv.device, inv_freq, k_cache, v_cache, q_norm, k_norm, pos_dev, out, ws)
+    with torch.cuda.device(qkv.device):
+        _lib.check(_lib.load().qz_attention_decode_qkv(
+            qkv.data_ptr(), _ptr(q_norm), _ptr(k_norm), inv_freq.data_ptr(), k_cache.data_ptr(),
+            v_cache.data_ptr(), out.data_ptr(), n_heads, nkv, hd, max_ctx, int(pos0),
+            _ptr(pos_dev), float(eps), float(scale), ws.data_ptr(), ws.numel(),
+            _stream_ptr(qkv.device)))
     return out
 
 

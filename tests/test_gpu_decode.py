@@ -120,7 +120,9 @@ def test_qk_rope(cuda_dev, qk_norm, nq, nkv, hd, M, pos0):
 
 @pytest.mark.parametrize("nq,nkv,hd,T,max_ctx", [(16, 8, 128, 513, 1024), (4, 2, 16, 1, 40),
                                                  (32, 8, 64, 64, 64), (8, 1, 128, 65, 200),
-                                                 (8, 8, 256, 300, 301)])
+                                                 (8, 8, 256, 300, 301), (16, 4, 256, 700, 4096),
+                                                 (64, 8, 128, 5000, 8192), (6, 2, 96, 100, 128),
+                                                 (16, 2, 256, 33, 64)])
 def test_attention_decode(cuda_dev, nq, nkv, hd, T, max_ctx):
     from quartz_b200 import device as qd
     g = torch.Generator().manual_seed(T * 7 + hd)
@@ -132,6 +134,47 @@ def test_attention_decode(cuda_dev, nq, nkv, hd, T, max_ctx):
     # device-held length (graph form): T = *T_dev + 1
     T_dev = torch.tensor([T - 1], dtype=torch.int64, device=cuda_dev)
     _close(qd.attention_decode(q, kc, vc, T_dev=T_dev, t_offset=1), ref, "attention T_dev")
+
+
+@pytest.mark.parametrize("qk_norm", [True, False])
+@pytest.mark.parametrize("nq,nkv,hd,pos,max_ctx", [(16, 8, 128, 512, 640), (32, 8, 64, 0, 16),
+                                                   (16, 4, 256, 1000, 1001), (4, 2, 16, 39, 52),
+                                                   (12, 2, 96, 70, 80)])
+def test_attention_decode_qkv(cuda_dev, qk_norm, nq, nkv, hd, pos, max_ctx):
+    """norm + RoPE + append + attention in one launch, against the separate ops'
+    references; positions other than pos untouched."""
+    from quartz_b200 import device as qd
+    from quartz_b200.model import ModelSpec, rope_inv_freq
+    g = torch.Generator().manual_seed(pos * 3 + hd)
+    spec = ModelSpec(arch="Qwen3ForCausalLM", hidden=64, layers=1, n_heads=nq, n_kv=nkv,
+                     head_dim=hd, inter=64, vocab=8, rope_theta=1e6, tie=True)
+    inv = torch.from_numpy(rope_inv_freq(spec)).to(cuda_dev)
+    qkv = torch.randn((nq + 2 * nkv) * hd, generator=g).to(cuda_dev)
+    qn = (1 + 0.1 * torch.randn(hd, generator=g)).to(cuda_dev) if qk_norm else None
+    kn = (1 + 0.1 * torch.randn(hd, generator=g)).to(cuda_dev) if qk_norm else None
+    kc = torch.randn(nkv, max_ctx, hd, generator=g).to(cuda_dev)
+    vc = torch.randn(nkv, max_ctx, hd, generator=g).to(cuda_dev)
+    kc0, vc0 = kc.clone(), vc.clone()
+    pos_dev = torch.tensor([pos], dtype=torch.int64, device=cuda_dev)
+    out = qd.attention_decode_qkv(qkv, inv, kc, vc, nq, pos_dev=pos_dev, q_norm=qn, k_norm=kn)
+    parts = qkv.view(nq + 2 * nkv, hd)
+    qh, kh, vh = parts[:nq], parts[nq:nq + nkv], parts[nq + nkv:]
+    if qk_norm:
+        qh, kh = _rms_ref(qh, qn, 1e-6), _rms_ref(kh, kn, 1e-6)
+    p = torch.tensor([float(pos)], device=cuda_dev)
+    qr = _rope_ref(qh[:, None], p, inv)[:, 0]
+    kr = _rope_ref(kh[:, None], p, inv)[:, 0]
+    _close(kc[:, pos], kr, "appended k")
+    assert torch.equal(vc[:, pos], vh)
+    keep = [t for t in range(max_ctx) if t != pos]
+    assert torch.equal(kc[:, keep], kc0[:, keep]) and torch.equal(vc[:, keep], vc0[:, keep])
+    kref, vref = kc0.clone(), vc0.clone()
+    kref[:, pos], vref[:, pos] = kr, vh
+    ref = _sdpa_ref(qr[:, None], kref[:, :pos + 1], vref[:, :pos + 1], hd ** -0.5, nq // nkv)
+    _close(out, ref.view(-1), "attention")
+    # twice in a row: the workspace's tickets were left ready
+    out2 = qd.attention_decode_qkv(qkv, inv, kc, vc, nq, pos_dev=pos_dev, q_norm=qn, k_norm=kn)
+    _close(out2, ref.view(-1), "attention, second call")
 
 
 @pytest.mark.parametrize("nq,nkv,hd,M,pos0", [(4, 2, 16, 5, 0), (32, 8, 64, 130, 0),
