@@ -216,6 +216,53 @@ int qz_attention_prefill(const float* q, const float* k_cache, const float* v_ca
 int qz_argmax(const float* logits, int64_t M, int64_t V, uint64_t* keys, int64_t* tokens,
               int64_t* pos_dev, int64_t pos_step, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Every decoder layer of one decode token in one persistent kernel.
+ * ------------------------------------------------------------------------ */
+
+/* Device pointers of one decoder layer (an array of these lives in device
+ * memory). int8 matrices are row-major with one fp32 scale per row; every
+ * pointer 16-byte aligned. qkv: q rows, k rows, v rows stacked; gu: gate rows
+ * then up rows (quartz/quantize.py:95-96). Norm weights fp32; q/k norms NULL
+ * for architectures without them (Llama). Caches [n_kv, max_ctx, head_dim]. */
+typedef struct {
+  const int8_t* qkv_q;   const float* qkv_s;    /* [(nq + 2 nkv) hd, H] */
+  const int8_t* o_q;     const float* o_s;      /* [H, nq hd] */
+  const int8_t* gu_q;    const float* gu_s;     /* [2 I, H] */
+  const int8_t* down_q;  const float* down_s;   /* [H, I] */
+  const float* in_norm_w;  const float* post_norm_w;   /* [H] */
+  const float* q_norm_w;   const float* k_norm_w;      /* [hd] or NULL */
+  float* k_cache;        float* v_cache;
+} qz_decoder_layer;
+
+/* Workspace bytes of qz_decode_layers (256-byte aligned, zeroed once before
+ * first use; calls sharing it must not overlap on the GPU). A call whose
+ * kernel reported a failed wait (qz_device_status) leaves it inconsistent:
+ * zero it again before the next call. */
+int qz_decode_step_workspace_bytes(int H, int I, int nq, int nkv, int hd, int64_t max_ctx,
+                                   int64_t* bytes);
+
+/* QZ_OK when qz_decode_layers runs these shapes on the current device, else
+ * QZ_ERR_UNSUPPORTED (use the per-op entry points instead). */
+int qz_decode_layers_supported(int H, int I, int nq, int nkv, int hd, int64_t max_ctx);
+
+/*
+ * One decode token through all n_layers layers of a Qwen3/Llama decoder
+ * (quartz/models/common.py:29-78, qwen3.py:31-45, llama.py:29-41) in one
+ * cooperative launch of one CTA per SM: embedding row of *token (per-row int8
+ * table, quartz/quantize.py:78-80), per layer RMSNorm -> q/k/v -> per-head
+ * q/k RMSNorm (if given) -> RoPE at position *pos_dev -> K/V append ->
+ * attention over positions [0, *pos_dev] -> o + residual -> RMSNorm -> fused
+ * SwiGLU MLP + residual; then the final RMSNorm into x_final [H], the
+ * lm_head input. The kernel waits at grid barriers between phases; each wait
+ * gives up after about a second (status word) instead of hanging.
+ */
+int qz_decode_layers(const qz_decoder_layer* layers, int n_layers, const int8_t* embed_q,
+                     const float* embed_s, int64_t vocab, const int64_t* token,
+                     const int64_t* pos_dev, const float* inv_freq, const float* norm_w,
+                     float* x_final, int H, int I, int nq, int nkv, int hd, int64_t max_ctx,
+                     float eps, float scale, void* ws, size_t ws_bytes, void* stream);
+
 /* Read the device status word of the current device into words[0..3]
  * ({error bits, first error site, block of first error, error count}); when
  * clear != 0 reset it to zero afterwards. Synchronises the device. */

@@ -9,6 +9,7 @@ the C ABI declared in include/quartz_b200.h.
 from __future__ import annotations
 
 import os
+import re
 import shutil
 import subprocess
 import sys
@@ -45,15 +46,49 @@ def up_to_date() -> bool:
     return all(p.stat().st_mtime <= t for p in sources())
 
 
+RESOURCES = PKG / "libquartz_b200.resources.txt"
+
+
+def parse_ptxas(log: str) -> dict[str, dict]:
+    """Per kernel: registers, static shared memory bytes, spill bytes (from
+    ptxas -v)."""
+    out: dict[str, dict] = {}
+    cur = None
+    for line in log.splitlines():
+        m = re.search(r"Compiling entry function '([^']+)'", line)
+        if m:
+            cur = m.group(1)
+            out[cur] = {"registers": 0, "smem": 0, "spill": 0}
+            continue
+        if cur is None:
+            continue
+        m = re.search(r"(\d+) bytes spill stores", line)
+        if m:
+            out[cur]["spill"] = int(m.group(1))
+        m = re.search(r"Used (\d+) registers", line)
+        if m:
+            out[cur]["registers"] = int(m.group(1))
+            m2 = re.search(r"(\d+) bytes smem", line)
+            out[cur]["smem"] = int(m2.group(1)) if m2 else 0
+    return out
+
+
 def build(force: bool = False, verbose: bool = False) -> Path:
     if not force and up_to_date():
         return OUT
-    cmd = [nvcc(), *NVCC_FLAGS, f"-I{REPO / 'include'}", f"-I{SRC}",
+    cmd = [nvcc(), "-Xptxas=-v", *NVCC_FLAGS, f"-I{REPO / 'include'}", f"-I{SRC}",
            "-o", str(OUT), str(SRC / "qz_api.cu")]
     if verbose:
-        cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd))
-    subprocess.run(cmd, check=True)
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        sys.stderr.write(r.stdout + r.stderr)
+        raise subprocess.CalledProcessError(r.returncode, cmd)
+    if verbose:
+        sys.stderr.write(r.stderr)
+    res = parse_ptxas(r.stderr)
+    RESOURCES.write_text("".join(f"{k} registers={v['registers']} smem={v['smem']} "
+                                 f"spill={v['spill']}\n" for k, v in sorted(res.items())))
     return OUT
 
 

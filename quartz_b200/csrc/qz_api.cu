@@ -14,6 +14,7 @@
 #include "qz_stream.cuh"
 #include "qz_tc_gemm.cuh"
 #include "qz_decode.cuh"
+#include "qz_decode_step.cuh"
 
 namespace {
 
@@ -798,6 +799,161 @@ int qz_attention_decode_qkv(const float* qkv, const float* q_norm_w, const float
   QZ_CUDA(cudaGetLastError());
   return attn_chunked(qs, k_cache, v_cache, out, nq, nkv, hd, max_ctx, pos_dev ? 0 : pos0 + 1,
                       pos_dev, 1, scale, part, st);
+}
+
+}  // extern "C"
+
+namespace {
+
+static_assert(sizeof(qz_decoder_layer) == sizeof(qz::mk::LayerW),
+              "qz_decoder_layer must match the kernel's layer record");
+
+// decode_layers workspace: [barrier count u64, tickets nkv u32, padded to 256 B]
+// [attention partials nkv * S_max * n_rep * (hd + 2) fp32] [activations
+// h, h2, qkv, attn, act fp32]
+struct StepLayout {
+  int64_t part_off, act_off, total;
+  int64_t h, h2, qkv, attn, act;   // float offsets within the activation block
+};
+
+StepLayout step_layout(int H, int I, int nq, int nkv, int hd, int64_t max_ctx) {
+  StepLayout l;
+  auto al = [](int64_t b) { return ((b + 255) / 256) * 256; };
+  const int64_t rows = qz::mk::kSlotBytes / (hd * 4);
+  const int64_t smax = qz::cdiv(max_ctx, rows);
+  l.part_off = al(8 + static_cast<int64_t>(nkv) * 4);
+  l.act_off = l.part_off + al(static_cast<int64_t>(nkv) * smax * (nq / nkv) * (hd + 2) * 4);
+  auto a64 = [](int64_t f) { return ((f + 63) / 64) * 64; };
+  l.h = 0;
+  l.h2 = l.h + a64(H);
+  l.qkv = l.h2 + a64(H);
+  l.attn = l.qkv + a64(static_cast<int64_t>(nq + 2 * nkv) * hd);
+  l.act = l.attn + a64(static_cast<int64_t>(nq) * hd);
+  l.total = l.act_off + (l.act + a64(I)) * 4;
+  return l;
+}
+
+int check_step_shape(const DeviceInfo& d, int H, int I, int nq, int nkv, int hd, int64_t max_ctx,
+                     const char* what) {
+  if (int rc = check_heads(nq, nkv, hd, what)) return rc;
+  if (H < 16 || I < 16 || max_ctx < 1) return fail(QZ_ERR_INVALID, std::string(what) + ": bad sizes");
+  const int64_t Ko = static_cast<int64_t>(nq) * hd;
+  if (hd != 64 && hd != 128 && hd != 256)
+    return fail(QZ_ERR_UNSUPPORTED, std::string(what) + ": head_dim must be 64, 128 or 256");
+  for (int64_t k : {static_cast<int64_t>(H), static_cast<int64_t>(I), Ko})
+    if (k % 16 || k > qz::mk::kMaxX || k > qz::mk::kSlotBytes)
+      return fail(QZ_ERR_UNSUPPORTED, std::string(what) +
+                                          ": row lengths must be multiples of 16 up to 16384");
+  const int n_rep = nq / nkv;
+  if (n_rep != 1 && n_rep != 2 && n_rep != 4 && n_rep != 8)
+    return fail(QZ_ERR_UNSUPPORTED, std::string(what) + ": query heads per kv head must be 1, 2, 4 or 8");
+  const int64_t smax = qz::cdiv(max_ctx, qz::mk::kSlotBytes / (hd * 4));
+  if (smax * n_rep + n_rep > qz::mk::kMaxX)
+    return fail(QZ_ERR_UNSUPPORTED, std::string(what) + ": context too long");
+  if (qz::cdiv(I, d.sms) > qz::mk::Smem::kMaxUnits)
+    return fail(QZ_ERR_UNSUPPORTED, std::string(what) + ": intermediate size too large");
+  if (!d.coop) return fail(QZ_ERR_UNSUPPORTED, std::string(what) + ": no cooperative launch");
+  if (d.smem_optin < qz::mk::Smem::total)
+    return fail(QZ_ERR_UNSUPPORTED, std::string(what) + ": not enough shared memory");
+  return QZ_OK;
+}
+
+template <int E>
+int launch_step(const DeviceInfo& d, const qz::mk::StepArgs& a, cudaStream_t st) {
+  auto fn = qz::mk::decode_layers_kernel<E>;
+  static std::atomic<int> attr_done{0};
+  if (!attr_done.load()) {
+    QZ_CUDA(cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 qz::mk::Smem::total));
+    attr_done.store(1);
+  }
+  int nb = 0;
+  QZ_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, fn, qz::mk::kThreadsMK,
+                                                        qz::mk::Smem::total));
+  if (nb < 1) return fail(QZ_ERR_UNSUPPORTED, "qz_decode_layers: kernel does not fit on an SM");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(d.sms));
+  cfg.blockDim = dim3(qz::mk::kThreadsMK);
+  cfg.dynamicSmemBytes = qz::mk::Smem::total;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  QZ_CUDA(cudaLaunchKernelEx(&cfg, fn, a));
+  return QZ_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int qz_decode_step_workspace_bytes(int H, int I, int nq, int nkv, int hd, int64_t max_ctx,
+                                   int64_t* bytes) {
+  if (!bytes) return fail(QZ_ERR_INVALID, "qz_decode_step_workspace_bytes: null bytes");
+  if (int rc = check_heads(nq, nkv, hd, "qz_decode_step_workspace_bytes")) return rc;
+  if (H < 1 || I < 1 || max_ctx < 1)
+    return fail(QZ_ERR_INVALID, "qz_decode_step_workspace_bytes: bad sizes");
+  *bytes = step_layout(H, I, nq, nkv, hd, max_ctx).total;
+  return QZ_OK;
+}
+
+int qz_decode_layers_supported(int H, int I, int nq, int nkv, int hd, int64_t max_ctx) {
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  return check_step_shape(*d, H, I, nq, nkv, hd, max_ctx, "qz_decode_layers");
+}
+
+int qz_decode_layers(const qz_decoder_layer* layers, int n_layers, const int8_t* embed_q,
+                     const float* embed_s, int64_t vocab, const int64_t* token,
+                     const int64_t* pos_dev, const float* inv_freq, const float* norm_w,
+                     float* x_final, int H, int I, int nq, int nkv, int hd, int64_t max_ctx,
+                     float eps, float scale, void* ws, size_t ws_bytes, void* stream) {
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  if (int rc = check_step_shape(*d, H, I, nq, nkv, hd, max_ctx, "qz_decode_layers")) return rc;
+  if (n_layers < 1 || !layers || !embed_q || !embed_s || !token || !pos_dev || !inv_freq ||
+      !norm_w || !x_final || !ws || vocab < 1)
+    return fail(QZ_ERR_INVALID, "qz_decode_layers: null pointer or empty model");
+  const StepLayout L = step_layout(H, I, nq, nkv, hd, max_ctx);
+  if (static_cast<int64_t>(ws_bytes) < L.total || !aligned_to(ws, 256))
+    return fail(QZ_ERR_INVALID, "qz_decode_layers: workspace too small or not 256-byte aligned");
+  char* w = static_cast<char*>(ws);
+  float* act = reinterpret_cast<float*>(w + L.act_off);
+  qz::mk::StepArgs a{};
+  a.layers = reinterpret_cast<const qz::mk::LayerW*>(layers);
+  a.n_layers = n_layers;
+  a.embed_q = embed_q;
+  a.embed_s = embed_s;
+  a.tok = token;
+  a.pos_dev = pos_dev;
+  a.inv_freq = inv_freq;
+  a.norm_w = norm_w;
+  a.h = act + L.h;
+  a.h2 = act + L.h2;
+  a.qkv = act + L.qkv;
+  a.attn = act + L.attn;
+  a.act = act + L.act;
+  a.x_final = x_final;
+  a.part = reinterpret_cast<float*>(w + L.part_off);
+  a.bar = reinterpret_cast<unsigned long long*>(w);
+  a.tickets = reinterpret_cast<unsigned*>(w + 8);
+  a.H = H;
+  a.I = I;
+  a.nq = nq;
+  a.nkv = nkv;
+  a.hd = hd;
+  a.max_ctx = max_ctx;
+  a.V = vocab;
+  a.eps = eps;
+  a.scale = scale;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  switch (hd) {
+    case 64: return launch_step<2>(*d, a, st);
+    case 128: return launch_step<4>(*d, a, st);
+    default: return launch_step<8>(*d, a, st);
+  }
 }
 
 int qz_attention_prefill(const float* q, const float* k_cache, const float* v_cache, float* out,

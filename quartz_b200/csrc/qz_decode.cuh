@@ -286,6 +286,58 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(
 // U positions per round; the 8 warps merge in shared memory into one partial
 // (acc[hd], max, sum) per query head, written to the workspace.
 // ---------------------------------------------------------------------------
+// Merge S partial softmaxes (acc[HD], max, sum per query head; layout
+// [S][NR][HD + 2]) of the NR query heads of one kv head into out [NR][HD]:
+// out = sum_c e^(m_c - M) acc_c / sum_c e^(m_c - M) l_c. Threads tid < NT
+// take part; sync() is their barrier; scratch holds NR * S + NR floats. The
+// per-chunk weights are computed once, and the accumulator loads of the final
+// sum are independent of one another so they overlap.
+template <int HD, int NR, int NT, class Sync>
+__device__ __forceinline__ void merge_partials(const float* part_g, int S, float* out_g,
+                                               float* scratch, int tid, Sync&& sync) {
+  constexpr int NW = NT / 32;
+  const int warp = tid >> 5, lane = tid & 31;
+  float* wf = scratch;            // [NR][S]
+  float* dn = scratch + NR * S;   // [NR]
+  for (int i = tid; i < NR * S; i += NT) {
+    const int r = i / S, c = i - r * S;
+    wf[i] = __ldcg(part_g + (static_cast<int64_t>(c) * NR + r) * (HD + 2) + HD);
+  }
+  sync();
+  for (int r = warp; r < NR; r += NW) {
+    float M = -INFINITY;
+    for (int c = lane; c < S; c += 32) M = fmaxf(M, wf[r * S + c]);
+    M = warp_max_f(M);
+    float den = 0.f;
+    for (int c = lane; c < S; c += 32) {
+      const float m = wf[r * S + c];
+      const float f = m == -INFINITY ? 0.f : expf(m - M);
+      den = fmaf(f, __ldcg(part_g + (static_cast<int64_t>(c) * NR + r) * (HD + 2) + HD + 1), den);
+      wf[r * S + c] = f;
+    }
+    den = warp_sum_f(den);
+    if (lane == 0) dn[r] = den;
+  }
+  sync();
+  constexpr int64_t stride = static_cast<int64_t>(NR) * (HD + 2);
+  for (int i = tid; i < NR * HD; i += NT) {
+    const int r = i / HD, d = i - r * HD;
+    const float* pr = part_g + r * (HD + 2) + d;
+    const float* w = wf + r * S;
+    float num = 0.f;
+    int c = 0;
+    for (; c + 8 <= S; c += 8) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = __ldcg(pr + (c + j) * stride);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) num = fmaf(w[c + j], v[j], num);
+    }
+    for (; c < S; ++c) num = fmaf(w[c], __ldcg(pr + c * stride), num);
+    out_g[r * HD + d] = num / dn[r];
+  }
+}
+
 struct AttnArgs {
   const float* in;        // QKV: qkv row [(nq + 2 nkv) hd]; else q [nq hd]
   const float* qn_w;      // [hd] or null
@@ -511,22 +563,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_fused_kernel(AttnArg
   if (!s_last) return;
   __threadfence();
   const float* gbase = a.part + static_cast<int64_t>(g) * S * NR * (HD + 2);
-  for (int i = threadIdx.x; i < NR * HD; i += kAttnThreads) {
-    const int r = i / HD, d = i - r * HD;
-    float M = -INFINITY, num = 0.f, den = 0.f;
-    for (int cc = 0; cc < S; ++cc) {
-      const float* pr = gbase + (cc * NR + r) * (HD + 2);
-      const float mc = __ldcg(pr + HD);
-      if (mc == -INFINITY) continue;
-      const float lc = __ldcg(pr + HD + 1), ac = __ldcg(pr + d);
-      const float Mn = fmaxf(M, mc);
-      const float fo = expf(M - Mn), fn = expf(mc - Mn);
-      num = num * fo + ac * fn;
-      den = den * fo + lc * fn;
-      M = Mn;
-    }
-    a.out[static_cast<int64_t>(g * NR + r) * HD + d] = num / den;
-  }
+  merge_partials<HD, NR, kAttnThreads>(gbase, S, a.out + static_cast<int64_t>(g) * NR * HD, red,
+                                       threadIdx.x, [] { __syncthreads(); });
   if (threadIdx.x == 0) a.tickets[g] = 0u;
 }
 

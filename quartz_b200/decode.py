@@ -57,7 +57,7 @@ class DecodeEngine:
     """
 
     def __init__(self, spec: ModelSpec, int8_weights: Mapping | Iterable, norms: Mapping,
-                 *, max_ctx: int, max_prefill: int = 512, device=None):
+                 *, max_ctx: int, max_prefill: int = 512, device=None, fused: bool = True):
         self.spec = spec
         self.dev = torch.device("cuda", qd.ensure_device(device))
         dev = self.dev
@@ -163,6 +163,33 @@ class DecodeEngine:
             self.gemm_ws = torch.empty(need, dtype=torch.uint8, device=dev)
         self._graph = None
         self._graph_steps = 0
+        self.fused = bool(fused) and self._setup_fused()
+
+    def _setup_fused(self) -> bool:
+        """Use the one-launch persistent kernel for all layers of a decode token
+        when the shapes allow it (per-row scales, head_dim 64/128/256, ...)."""
+        S, lib = self.spec, self.lib
+        per_row = all(t.shape[1] == 1 for L in self.layers
+                      for t in (L.qkv_s, L.o_s, L.gu_s, L.down_s)) and self.embed_s.shape[1] == 1
+        if not per_row:
+            return False
+        with torch.cuda.device(self.dev):
+            if lib.qz_decode_layers_supported(S.hidden, S.inter, S.n_heads, S.n_kv, S.head_dim,
+                                              self.max_ctx) != 0:
+                return False
+            b = ctypes.c_int64(0)
+            _lib.check(lib.qz_decode_step_workspace_bytes(S.hidden, S.inter, S.n_heads, S.n_kv,
+                                                          S.head_dim, self.max_ctx,
+                                                          ctypes.byref(b)))
+        self.step_ws = torch.zeros(b.value, dtype=torch.uint8, device=self.dev)
+        # qz_decoder_layer records (14 pointers each) in device memory
+        recs = []
+        for li, L in enumerate(self.layers):
+            recs.append([t.data_ptr() if t is not None else 0 for t in (
+                L.qkv_q, L.qkv_s, L.o_q, L.o_s, L.gu_q, L.gu_s, L.down_q, L.down_s, L.in_w,
+                L.post_w, L.qn_w, L.kn_w, self.k_cache[li], self.v_cache[li])])
+        self.layer_recs = torch.tensor(recs, dtype=torch.int64).to(self.dev)
+        return True
 
     # ------------------------------------------------------------------ state
     def reset(self, pos: int = 0) -> None:
@@ -206,6 +233,17 @@ class DecodeEngine:
         H, hd, nq, nkv = S.hidden, S.head_dim, S.n_heads, S.n_kv
         p = lambda t: t.data_ptr()  # noqa: E731
         h_a, h_b, xn = p(self.h_a), p(self.h_b), p(self.xn)
+        if self.fused:
+            chk(lib.qz_decode_layers(p(self.layer_recs), S.layers, p(self.embed_q), p(self.embed_s),
+                                     S.vocab, p(self.tok), p(self.pos_dev), p(self.inv_freq),
+                                     p(self.norm_w), xn, H, S.inter, nq, nkv, hd, self.max_ctx,
+                                     S.eps, self.attn_scale, p(self.step_ws),
+                                     self.step_ws.numel(), st))
+            chk(lib.qz_gemv_w8(p(self.lm_q), p(self.lm_s), self.lm_s.shape[1], xn,
+                               p(self.logits), S.vocab, H, None, st))
+            chk(lib.qz_argmax(p(self.logits), 1, S.vocab, p(self.keys), p(self.tok),
+                              p(self.pos_dev), 1, st))
+            return
         chk(lib.qz_embed_gather(p(self.embed_q), p(self.embed_s), self.embed_s.shape[1],
                                 p(self.tok), 1, S.vocab, H, h_a, st))
         for li, L in enumerate(self.layers):
@@ -231,6 +269,8 @@ class DecodeEngine:
                           1, st))
 
     def _launches_per_token(self) -> int:
+        if self.fused:
+            return 4   # decode_layers, lm_head GEMV, argmax + finish
         # embed + per layer (rmsnorm, qkv, attention, o, rmsnorm, mlp) + norm, lm, argmax x2;
         # attention is one launch for the head shapes of the fused kernel
         return 1 + 6 * self.spec.layers + 4

@@ -54,6 +54,17 @@ CASES = [
                   num_key_value_heads=2, head_dim=16, intermediate_size=128, vocab_size=64,
                   rope_theta=10000.0, tie_word_embeddings=True),
          start="kv", kv_len=40, first=7, steps=12),
+    # small models with the head sizes of the real ones (64 / 128)
+    dict(id="qwen3_small_kv", arch="Qwen3ForCausalLM",
+         cfg=dict(hidden_size=256, num_hidden_layers=3, num_attention_heads=4,
+                  num_key_value_heads=2, head_dim=64, intermediate_size=512, vocab_size=1000,
+                  rope_theta=1000000.0, tie_word_embeddings=True),
+         start="kv", kv_len=100, first=3, steps=24),
+    dict(id="llama_small_prompt", arch="LlamaForCausalLM",
+         cfg=dict(hidden_size=512, num_hidden_layers=2, num_attention_heads=8,
+                  num_key_value_heads=2, head_dim=128, intermediate_size=1024, vocab_size=2000,
+                  rope_theta=500000.0, tie_word_embeddings=False, rope_scaling=LLAMA3_SCALING),
+         start="prompt_rng", prompt_seed=11, prompt_len=37, steps=24),
     # Qwen3-0.6B architecture: 512 prefilled KV positions, 128 greedy tokens
     dict(id="qwen3_0p6b_kv512", arch="Qwen3ForCausalLM",
          cfg=dict(hidden_size=1024, num_hidden_layers=28, num_attention_heads=16,

@@ -221,14 +221,14 @@ def _golden(cid, key):
         return z[f"{cid}__{key}"]
 
 
-def _engine(case, extra_ctx=0):
+def _engine(case, extra_ctx=0, fused=True):
     from quartz_b200.decode import DecodeEngine
     from quartz_b200.model import ModelSpec, norm_weights, random_int8_weights
     spec = ModelSpec.from_hf(case["cfg"], case["arch"])
     start = case.get("kv_len") or len(case["prompt"])
     eng = DecodeEngine(spec, random_int8_weights(spec), norm_weights(spec),
                        max_ctx=start + case["steps"] + extra_ctx,
-                       max_prefill=max(2, len(case.get("prompt", [])) or 2))
+                       max_prefill=max(2, len(case.get("prompt", [])) or 2), fused=fused)
     return spec, eng
 
 
@@ -241,22 +241,48 @@ def _run(case, eng, graph, unroll=8):
     return [t0] + eng.generate(t0, case["steps"] - 1, graph=graph, unroll=unroll)
 
 
-@pytest.mark.parametrize("cid", ["qwen3_tiny_prompt", "llama_tiny_prompt", "qwen3_tiny_kv"])
-def test_engine_tiny(cuda_dev, cid):
+@pytest.mark.parametrize("cid", ["qwen3_tiny_prompt", "llama_tiny_prompt", "qwen3_tiny_kv",
+                                 "qwen3_small_kv", "llama_small_prompt"])
+@pytest.mark.parametrize("fused", [True, False])
+def test_engine_small(cuda_dev, cid, fused):
+    """Greedy tokens of small models, eager and graph replay; every eager step's
+    top-8 logits against the reference's (1e-4 of the largest)."""
+    from quartz_b200.model import seeded_kv
     case = _cases()[cid]
     gold = _golden(cid, "tokens").tolist()
-    _, eng = _engine(case)
-    assert _run(case, eng, graph=False) == gold, "eager"
+    top_ids = _golden(cid, "top_ids")
+    top_vals = _golden(cid, "top_vals")
+    _, eng = _engine(case, fused=fused)
+    if fused and case["cfg"]["head_dim"] in (64, 128, 256):
+        assert eng.fused, "the one-launch decode kernel should take these shapes"
+    if case["start"] == "kv":
+        eng.load_kv(seeded_kv(eng.spec, case["kv_len"]))
+        tok = case["first"]
+        toks = []
+    else:
+        tok = eng.prefill(case["prompt"])
+        toks = [tok]
+        _close(eng.logits.cpu()[torch.from_numpy(top_ids[0])], torch.from_numpy(top_vals[0]),
+               f"{cid} prefill logits")
+    while len(toks) < case["steps"]:
+        tok = eng.decode(tok)
+        step = len(toks)
+        _close(eng.logits.cpu()[torch.from_numpy(top_ids[step])],
+               torch.from_numpy(top_vals[step]), f"{cid} step {step} logits")
+        toks.append(tok)
+    assert toks == gold, "eager"
     eng.reset(0)
     assert _run(case, eng, graph=True, unroll=5) == gold, "graph"
 
 
-def test_engine_qwen3_0p6b_kv512(cuda_dev):
+@pytest.mark.parametrize("fused", [True, False])
+def test_engine_qwen3_0p6b_kv512(cuda_dev, fused):
     """The all-int8 Qwen3-0.6B decode workload: 512 prefilled positions, 128
     greedy tokens through the graph replay; the first step's top-8 logits too."""
     case = _cases()["qwen3_0p6b_kv512"]
     gold = _golden(case["id"], "tokens").tolist()
-    spec, eng = _engine(case)
+    spec, eng = _engine(case, fused=fused)
+    assert eng.fused == fused
     from quartz_b200.model import seeded_kv
     eng.load_kv(seeded_kv(spec, case["kv_len"]))
     first = eng.generate(case["first"], 1, graph=False)

@@ -132,3 +132,16 @@ def test_numpy_api_validates_before_touching_the_gpu():
     with pytest.raises(TypeError):
         kernels.w8a32_gemv(np.zeros((4, 64), np.float32), np.ones((4, 1), np.float32),
                            np.zeros(64, np.float32), np.zeros(4, np.float32))
+
+
+def test_kernel_resources():
+    """ptxas figures of the built library: no register spills, and at most 256
+    bytes of static shared memory per kernel (the launch code reserves 256
+    bytes below the opt-in maximum for it)."""
+    from quartz_b200 import build
+    if not build.RESOURCES.exists():
+        pytest.skip("library built without resource figures")
+    rows = build.RESOURCES.read_text().split("\n")
+    bad = [r for r in rows if r and (int(r.split("smem=")[1].split()[0]) > 256
+                                     or int(r.split("spill=")[1]) > 0)]
+    assert not bad, bad
