@@ -242,8 +242,9 @@ typedef struct {
 int qz_decode_step_workspace_bytes(int H, int I, int nq, int nkv, int hd, int64_t max_ctx,
                                    int64_t* bytes);
 
-/* QZ_OK when qz_decode_layers runs these shapes on the current device, else
- * QZ_ERR_UNSUPPORTED (use the per-op entry points instead). */
+/* QZ_OK when qz_decode_layers runs these shapes on the current device (per-row
+ * scales, head_dim 64 or 128, 1/2/4/8 query heads per kv head, rows of at most
+ * 16 KB, ...), else QZ_ERR_UNSUPPORTED (use the per-op entry points instead). */
 int qz_decode_layers_supported(int H, int I, int nq, int nkv, int hd, int64_t max_ctx);
 
 /*
@@ -256,12 +257,17 @@ int qz_decode_layers_supported(int H, int I, int nq, int nkv, int hd, int64_t ma
  * SwiGLU MLP + residual; then the final RMSNorm into x_final [H], the
  * lm_head input. The kernel waits at grid barriers between phases; each wait
  * gives up after about a second (status word) instead of hanging.
+ * trace: NULL, or device uint64 [n_SMs][1 + 10 n_layers] that receives
+ * %globaltimer stamps per CTA: launch start, then per layer and phase
+ * (qkv, attention, o, gate/up, down) the end of its work and the end of the
+ * grid barrier that follows.
  */
 int qz_decode_layers(const qz_decoder_layer* layers, int n_layers, const int8_t* embed_q,
                      const float* embed_s, int64_t vocab, const int64_t* token,
                      const int64_t* pos_dev, const float* inv_freq, const float* norm_w,
                      float* x_final, int H, int I, int nq, int nkv, int hd, int64_t max_ctx,
-                     float eps, float scale, void* ws, size_t ws_bytes, void* stream);
+                     float eps, float scale, void* ws, size_t ws_bytes, uint64_t* trace,
+                     void* stream);
 
 /* Read the device status word of the current device into words[0..3]
  * ({error bits, first error site, block of first error, error count}); when

@@ -54,7 +54,7 @@ SIGNATURES = {
     "qz_decode_layers_supported": ([_int, _int, _int, _int, _int, _i64], _int),
     "qz_decode_layers": ([_vp, _int, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _int, _int, _int,
                           _int, _int, _i64, ctypes.c_float, ctypes.c_float, _vp, ctypes.c_size_t,
-                          _vp], _int),
+                          _vp, _vp], _int),
     "qz_device_status": ([ctypes.POINTER(ctypes.c_uint32), _int], _int),
     "qz_sync": ([_vp], _int),
 }

@@ -838,8 +838,8 @@ int check_step_shape(const DeviceInfo& d, int H, int I, int nq, int nkv, int hd,
   if (int rc = check_heads(nq, nkv, hd, what)) return rc;
   if (H < 16 || I < 16 || max_ctx < 1) return fail(QZ_ERR_INVALID, std::string(what) + ": bad sizes");
   const int64_t Ko = static_cast<int64_t>(nq) * hd;
-  if (hd != 64 && hd != 128 && hd != 256)
-    return fail(QZ_ERR_UNSUPPORTED, std::string(what) + ": head_dim must be 64, 128 or 256");
+  if (hd != 64 && hd != 128)
+    return fail(QZ_ERR_UNSUPPORTED, std::string(what) + ": head_dim must be 64 or 128");
   for (int64_t k : {static_cast<int64_t>(H), static_cast<int64_t>(I), Ko})
     if (k % 16 || k > qz::mk::kMaxX || k > qz::mk::kSlotBytes)
       return fail(QZ_ERR_UNSUPPORTED, std::string(what) +
@@ -848,8 +848,11 @@ int check_step_shape(const DeviceInfo& d, int H, int I, int nq, int nkv, int hd,
   if (n_rep != 1 && n_rep != 2 && n_rep != 4 && n_rep != 8)
     return fail(QZ_ERR_UNSUPPORTED, std::string(what) + ": query heads per kv head must be 1, 2, 4 or 8");
   const int64_t smax = qz::cdiv(max_ctx, qz::mk::kSlotBytes / (hd * 4));
-  if (smax * n_rep + n_rep > qz::mk::kMaxX)
+  if (2 * smax * n_rep + n_rep > qz::mk::kMaxX)
     return fail(QZ_ERR_UNSUPPORTED, std::string(what) + ": context too long");
+  const int64_t nA = qz::cdiv(static_cast<int64_t>(nq + 2 * nkv) * hd, d.sms);
+  if (nA + 5 * qz::cdiv(H, d.sms) + 2 * qz::cdiv(I, d.sms) > qz::mk::Smem::kMaxPre)
+    return fail(QZ_ERR_UNSUPPORTED, std::string(what) + ": layer too large for the row caches");
   if (qz::cdiv(I, d.sms) > qz::mk::Smem::kMaxUnits)
     return fail(QZ_ERR_UNSUPPORTED, std::string(what) + ": intermediate size too large");
   if (!d.coop) return fail(QZ_ERR_UNSUPPORTED, std::string(what) + ": no cooperative launch");
@@ -909,7 +912,8 @@ int qz_decode_layers(const qz_decoder_layer* layers, int n_layers, const int8_t*
                      const float* embed_s, int64_t vocab, const int64_t* token,
                      const int64_t* pos_dev, const float* inv_freq, const float* norm_w,
                      float* x_final, int H, int I, int nq, int nkv, int hd, int64_t max_ctx,
-                     float eps, float scale, void* ws, size_t ws_bytes, void* stream) {
+                     float eps, float scale, void* ws, size_t ws_bytes, uint64_t* trace,
+                     void* stream) {
   DeviceInfo* d = nullptr;
   if (int rc = device_info(&d)) return rc;
   if (int rc = check_step_shape(*d, H, I, nq, nkv, hd, max_ctx, "qz_decode_layers")) return rc;
@@ -948,12 +952,9 @@ int qz_decode_layers(const qz_decoder_layer* layers, int n_layers, const int8_t*
   a.V = vocab;
   a.eps = eps;
   a.scale = scale;
+  a.trace = reinterpret_cast<unsigned long long*>(trace);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  switch (hd) {
-    case 64: return launch_step<2>(*d, a, st);
-    case 128: return launch_step<4>(*d, a, st);
-    default: return launch_step<8>(*d, a, st);
-  }
+  return hd == 64 ? launch_step<2>(*d, a, st) : launch_step<4>(*d, a, st);
 }
 
 int qz_attention_prefill(const float* q, const float* k_cache, const float* v_cache, float* out,

@@ -289,19 +289,22 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(
 // Merge S partial softmaxes (acc[HD], max, sum per query head; layout
 // [S][NR][HD + 2]) of the NR query heads of one kv head into out [NR][HD]:
 // out = sum_c e^(m_c - M) acc_c / sum_c e^(m_c - M) l_c. Threads tid < NT
-// take part; sync() is their barrier; scratch holds NR * S + NR floats. The
-// per-chunk weights are computed once, and the accumulator loads of the final
-// sum are independent of one another so they overlap.
+// take part; sync() is their barrier; scratch holds 2 NR S + NR floats. Two
+// dependent rounds of L2 loads: all maxima and sums at once, then the
+// accumulators, whose loads are independent of one another so they overlap.
 template <int HD, int NR, int NT, class Sync>
 __device__ __forceinline__ void merge_partials(const float* part_g, int S, float* out_g,
                                                float* scratch, int tid, Sync&& sync) {
   constexpr int NW = NT / 32;
   const int warp = tid >> 5, lane = tid & 31;
-  float* wf = scratch;            // [NR][S]
-  float* dn = scratch + NR * S;   // [NR]
+  float* wf = scratch;                // [NR][S] maxima, then weights
+  float* lf = scratch + NR * S;       // [NR][S] sums
+  float* dn = scratch + 2 * NR * S;   // [NR]
   for (int i = tid; i < NR * S; i += NT) {
     const int r = i / S, c = i - r * S;
-    wf[i] = __ldcg(part_g + (static_cast<int64_t>(c) * NR + r) * (HD + 2) + HD);
+    const float* pr = part_g + (static_cast<int64_t>(c) * NR + r) * (HD + 2) + HD;
+    wf[i] = __ldcg(pr);
+    lf[i] = __ldcg(pr + 1);
   }
   sync();
   for (int r = warp; r < NR; r += NW) {
@@ -312,7 +315,7 @@ __device__ __forceinline__ void merge_partials(const float* part_g, int S, float
     for (int c = lane; c < S; c += 32) {
       const float m = wf[r * S + c];
       const float f = m == -INFINITY ? 0.f : expf(m - M);
-      den = fmaf(f, __ldcg(part_g + (static_cast<int64_t>(c) * NR + r) * (HD + 2) + HD + 1), den);
+      den = fmaf(f, lf[r * S + c], den);
       wf[r * S + c] = f;
     }
     den = warp_sum_f(den);

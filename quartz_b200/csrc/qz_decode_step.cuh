@@ -30,7 +30,7 @@
 // kWaitLimitNs, record ERR_* in the status word, and the CTA drains its copies
 // and returns. Requires: one CTA per SM resident for the whole grid
 // (cooperative launch), per-row scales, row lengths multiples of 16 bytes and
-// at most one ring slot, head_dim 64/128/256.
+// at most one ring slot, head_dim 64 or 128.
 #pragma once
 
 #include "qz_decode.cuh"
@@ -42,7 +42,9 @@ namespace mk {
 
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumers = 32 * kConsumerWarps;
-constexpr int kThreadsMK = kConsumers + 32;   // + the producer warp
+// + the producer warp. Nine warps put three on some SM sub-partition (16384
+// registers each), so a thread may use at most 168 registers.
+constexpr int kThreadsMK = kConsumers + 32;
 constexpr int kSlotBytes = 16384;
 constexpr int kSlots = 8;
 constexpr int kMaxX = 16384;                 // longest staged activation (floats)
@@ -75,6 +77,7 @@ struct StepArgs {
   float* part;             // attention partials [nkv][S][NR][hd + 2]
   unsigned* tickets;       // [nkv], zero between launches
   unsigned long long* bar; // grid-barrier arrival count, zero before the first launch
+  unsigned long long* trace;  // null, or [gridDim.x][1 + 10 * n_layers] %globaltimer stamps
   int H, I, nq, nkv, hd;
   int64_t max_ctx, V;
   float eps, scale;
@@ -92,7 +95,12 @@ struct Smem {
   static constexpr int sc = qs + 8 * 256 * 4;
   static constexpr int kvn = sc + 8 * 64 * 4;
   static constexpr int red = kvn + 2 * 256 * 4;
-  static constexpr int bars = red + 64 * 4;                      // full[kSlots], empty[kSlots]
+  // per-layer row scales and residual slices of this CTA: A | C | gate | up | E | res C | res E
+  static constexpr int kMaxPre = 2048;
+  static constexpr int pre = red + 64 * 4;
+  // constants: RoPE inverse frequencies [128], this layer's q/k norm weights [256] each
+  static constexpr int cst = pre + kMaxPre * 4;
+  static constexpr int bars = cst + 640 * 4;                     // full[kSlots], empty[kSlots]
   static constexpr int flags = bars + 2 * kSlots * 8;
   static constexpr int total = flags + 64;
 };
@@ -167,8 +175,9 @@ __device__ __forceinline__ void consumer_sync() { named_bar_sync(1, kConsumers);
 
 // Grid barrier among the consumer warps of every CTA (the producer never
 // joins) on a monotonically increasing 64-bit arrival count: a CTA adds 1 with
-// a fire-and-forget release reduction and waits until the count reaches
-// base + k * P for its k-th barrier. No reset round trips; a launch that
+// a fire-and-forget reduction and waits until the count reaches
+// base + k * P for its k-th barrier (fence.acq_rel + relaxed reduction on
+// arrival, acquire loads while waiting). No reset round trips; a launch that
 // completes all its barriers leaves the count at a multiple of (barriers per
 // launch) * P, which is how the next launch recovers its base. Returns false
 // on timeout (status recorded); the count is then out of step and the
@@ -179,8 +188,8 @@ __device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long
   return v;
 }
 
-__device__ __forceinline__ void red_release_add_u64(unsigned long long* p, unsigned long long v) {
-  asm volatile("red.release.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+__device__ __forceinline__ void red_relaxed_add_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("red.relaxed.gpu.global.add.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
 struct GridBar {
@@ -194,8 +203,10 @@ __device__ __forceinline__ bool consumer_grid_barrier(GridBar& gb, unsigned* s_f
   if (tid == 0) {
     unsigned ok = 1u;
     gb.target += gridDim.x;
-    __threadfence();
-    red_release_add_u64(gb.count, 1ull);
+    // the CTA's writes (ordered before by the named barrier) are released at
+    // gpu scope by this fence, then the arrival is a relaxed reduction
+    asm volatile("fence.acq_rel.gpu;" ::: "memory");
+    red_relaxed_add_u64(gb.count, 1ull);
     if (ld_acquire_u64(gb.count) < gb.target) {
       const unsigned long long t0 = globaltimer();
       while (ld_acquire_u64(gb.count) < gb.target) {
@@ -229,33 +240,53 @@ __device__ __forceinline__ float ld_act(const float* p) {
   return COHERENT ? __ldcg(p) : *p;
 }
 
-// xs (stage_x layout) = RMSNorm(src) * w over n elements (quartz/ops.py:24-32).
-// src was written by other CTAs earlier in this kernel: read through L2, once
-// (held in registers) when n <= kRegX * kConsumers.
-constexpr int kRegX = 16;
+// Activations are staged in shared memory in the layout load_x16 reads,
+// float index ((j / 4) * nch + c) * 4 + j % 4 for element 16 c + j (nch =
+// n / 16), so that lane-consecutive 16-element chunks are conflict-free.
+// The staging walks the DESTINATION in thread order (conflict-free stores):
+// destination o = j4 * 4 nch + rem holds element 16 (rem / 4) + 4 j4 + rem % 4.
+__device__ __forceinline__ int staged_src(int j4, int rem) {
+  return (rem >> 2) * 16 + j4 * 4 + (rem & 3);
+}
+
+// xs = src (n floats written by other CTAs earlier in this kernel: L2 reads)
+__device__ __forceinline__ void stage_act(float* xs, const float* src, int n, int tid) {
+  const int nch4 = n / 4;
+#pragma unroll
+  for (int j4 = 0; j4 < 4; ++j4)
+    for (int rem = tid; rem < nch4; rem += kConsumers)
+      xs[j4 * nch4 + rem] = __ldcg(src + staged_src(j4, rem));
+}
+
+// xs = RMSNorm(src) * w (quartz/ops.py:24-32), src and w read in ONE round of
+// loads (values held in registers) when n <= 4 kRegX kConsumers.
+constexpr int kRegX = 2;   // per j4
 __device__ __forceinline__ void stage_rmsnorm(float* xs, const float* src, const float* w, int n,
                                               float eps, float* red, int tid) {
-  const int64_t nch = n / 16;
-  auto put = [&](int i, float v) {
-    const int c = i >> 4, j = i & 15;
-    xs[((j >> 2) * nch + c) * 4 + (j & 3)] = v;
-  };
-  if (n <= kRegX * kConsumers) {
-    float v[kRegX];
+  const int nch4 = n / 4;
+  if (nch4 <= kRegX * kConsumers) {
+    float v[4][kRegX], wv[4][kRegX];
     float ss = 0.f;
 #pragma unroll
-    for (int j = 0; j < kRegX; ++j) {
-      const int i = tid + j * kConsumers;
-      v[j] = i < n ? __ldcg(src + i) : 0.f;
-      ss = fmaf(v[j], v[j], ss);
-    }
+    for (int j4 = 0; j4 < 4; ++j4)
+#pragma unroll
+      for (int k = 0; k < kRegX; ++k) {
+        const int rem = tid + k * kConsumers;
+        const bool in = rem < nch4;
+        const int i = staged_src(j4, rem);
+        v[j4][k] = in ? __ldcg(src + i) : 0.f;
+        wv[j4][k] = in ? w[i] : 0.f;
+        ss = fmaf(v[j4][k], v[j4][k], ss);
+      }
     ss = consumer_sum(ss, red, tid);
     const float r = 1.0f / sqrtf(ss / static_cast<float>(n) + eps);
 #pragma unroll
-    for (int j = 0; j < kRegX; ++j) {
-      const int i = tid + j * kConsumers;
-      if (i < n) put(i, v[j] * r * w[i]);
-    }
+    for (int j4 = 0; j4 < 4; ++j4)
+#pragma unroll
+      for (int k = 0; k < kRegX; ++k) {
+        const int rem = tid + k * kConsumers;
+        if (rem < nch4) xs[j4 * nch4 + rem] = v[j4][k] * r * wv[j4][k];
+      }
     return;
   }
   float ss = 0.f;
@@ -265,10 +296,61 @@ __device__ __forceinline__ void stage_rmsnorm(float* xs, const float* src, const
   }
   ss = consumer_sum(ss, red, tid);
   const float r = 1.0f / sqrtf(ss / static_cast<float>(n) + eps);
-  for (int i = tid; i < n; i += kConsumers) put(i, __ldcg(src + i) * r * w[i]);
+#pragma unroll
+  for (int j4 = 0; j4 < 4; ++j4)
+    for (int rem = tid; rem < nch4; rem += kConsumers) {
+      const int i = staged_src(j4, rem);
+      xs[j4 * nch4 + rem] = __ldcg(src + i) * r * w[i];
+    }
 }
 
 // One row of K bytes in shared memory against the staged activations.
+__device__ __forceinline__ float row_dot(const uint8_t* row, const uint8_t* xs, int K, int lane);
+
+// Two rows at once (the activations are read once for both).
+__device__ __forceinline__ void row_dot2(const uint8_t* row0, const uint8_t* row1,
+                                         const uint8_t* xs, int K, int lane, float& d0,
+                                         float& d1) {
+  const int64_t nch = K / 16;
+  f2_t a0 = 0ull, a1 = 0ull;
+  for (int c = lane; c < K / 16; c += 32) {
+    const uint4 q0 = *reinterpret_cast<const uint4*>(row0 + c * 16);
+    const uint4 q1 = *reinterpret_cast<const uint4*>(row1 + c * 16);
+    f2_t xv[8];
+    load_x16(xs, nch, c, xv);
+    dot16_acc(q0, xv, a0);
+    dot16_acc(q1, xv, a1);
+  }
+  const float2 s0 = f2_unpack(a0), s1 = f2_unpack(a1);
+  float v0 = s0.x + s0.y, v1 = s1.x + s1.y;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    v0 += __shfl_xor_sync(0xffffffffu, v0, o);
+    v1 += __shfl_xor_sync(0xffffffffu, v1, o);
+  }
+  d0 = v0;
+  d1 = v1;
+}
+
+// The rows [0, rows) of a ring slot (row length K) against the staged
+// activations: warp w takes rows 2w, 2w + 1, 2w + 16, ...; emit(i, dot) runs
+// in lane 0 for every row.
+template <class F>
+__device__ __forceinline__ void chunk_rows(const uint8_t* slot, int rows, int K, const float* xs,
+                                           int warp, int lane, F&& emit) {
+  const uint8_t* x8 = reinterpret_cast<const uint8_t*>(xs);
+  for (int r = 2 * warp; r < rows; r += 2 * kConsumerWarps) {
+    if (r + 1 < rows) {
+      float d0, d1;
+      row_dot2(slot + r * K, slot + (r + 1) * K, x8, K, lane, d0, d1);
+      if (lane == 0) { emit(r, d0); emit(r + 1, d1); }
+    } else {
+      const float d = row_dot(slot + r * K, x8, K, lane);
+      if (lane == 0) emit(r, d);
+    }
+  }
+}
+
 __device__ __forceinline__ float row_dot(const uint8_t* row, const uint8_t* xs, int K, int lane) {
   const int64_t nch = K / 16;
   f2_t acc = 0ull;
@@ -296,7 +378,7 @@ __device__ __forceinline__ void merge_group(const float* part_g, int S, int NR, 
 }
 
 template <int E>
-__global__ void __maxnreg__(224) decode_layers_kernel(const StepArgs a) {
+__global__ void __launch_bounds__(kThreadsMK, 1) decode_layers_kernel(const StepArgs a) {
   constexpr int HD = 32 * E;
   extern __shared__ __align__(128) uint8_t smem[];  // 128: the alignment every kernel here declares
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -307,6 +389,10 @@ __global__ void __maxnreg__(224) decode_layers_kernel(const StepArgs a) {
   float* sc = reinterpret_cast<float*>(smem + Smem::sc);
   float* kvn = reinterpret_cast<float*>(smem + Smem::kvn);
   float* red = reinterpret_cast<float*>(smem + Smem::red);
+  float* pre = reinterpret_cast<float*>(smem + Smem::pre);
+  float* invf = reinterpret_cast<float*>(smem + Smem::cst);
+  float* qn_s = invf + 128;
+  float* kn_s = qn_s + 256;
   const uint32_t bars = smem_u32(smem + Smem::bars);
   auto full_bar = [&](int s) { return bars + 8u * s; };
   auto empty_bar = [&](int s) { return bars + 8u * (kSlots + s); };
@@ -397,55 +483,106 @@ __global__ void __maxnreg__(224) decode_layers_kernel(const StepArgs a) {
     const unsigned long long per_launch = 5ull * a.n_layers * gridDim.x;
     gbar.target = ld_acquire_u64(a.bar) / per_launch * per_launch;
   }
+  // optional phase trace: stamp k of this CTA (consumer thread 0)
+  const int n_stamps = 1 + 10 * a.n_layers;
+  auto stamp = [&](int k) {
+    if (a.trace && tid == 0) a.trace[static_cast<int64_t>(blockIdx.x) * n_stamps + k] = globaltimer();
+  };
+  stamp(0);
   int64_t tok = *a.tok;
   tok = tok < 0 ? 0 : (tok >= a.V ? a.V - 1 : tok);   // validated on the host; stay in bounds
 
+  for (int i = tid; i < hd / 2; i += kConsumers) invf[i] = a.inv_freq[i];
+  constexpr int KP = kSlotBytes / (HD * 4) / kConsumerWarps;   // K/V rows per warp per chunk
   for (int l = 0; l < a.n_layers && ok; ++l) {
     const LayerW& L = a.layers[l];
+    // This CTA's rows of every matrix of the layer (C and E share the
+    // H-split). Their scales, the residual rows phase C adds and the q/k norm
+    // weights are loaded into shared memory now, beside the activation
+    // staging, so that no output row waits on a global load after its dot
+    // product.
+    int64_t a0, a1, c0, c1, d0, d1;
+    split_range(static_cast<int64_t>(nq + 2 * nkv) * hd, P, b, a0, a1);
+    split_range(H, P, b, c0, c1);
+    split_range(I, P, b, d0, d1);
+    const int nA = static_cast<int>(a1 - a0), nC = static_cast<int>(c1 - c0);
+    const int nD = static_cast<int>(d1 - d0);
+    float* sA = pre;
+    float* sC = sA + nA;
+    float* sG = sC + nC;
+    float* sU = sG + nD;
+    float* sE = sU + nD;
+    float* rC = sE + nC;
+    float* rE = rC + nC;
+    {
+      const int n_pre = nA + 4 * nC + 2 * nD;   // everything but rE
+      for (int i = tid; i < n_pre; i += kConsumers) {
+        float v;
+        int j = i;
+        if (j < nA) v = __ldg(L.qkv_s + a0 + j);
+        else if ((j -= nA) < nC) v = __ldg(L.o_s + c0 + j);
+        else if ((j -= nC) < nD) v = __ldg(L.gu_s + d0 + j);
+        else if ((j -= nD) < nD) v = __ldg(L.gu_s + I + d0 + j);
+        else if ((j -= nD) < nC) v = __ldg(L.down_s + c0 + j);
+        else {
+          j -= nC;   // residual of phase C: h (layer 0: the embedding row)
+          v = l == 0 ? static_cast<float>(a.embed_q[tok * H + c0 + j]) * a.embed_s[tok]
+                     : __ldcg(a.h + c0 + j);
+        }
+        pre[i] = v;
+      }
+      if (L.qn_w)
+        for (int i = tid; i < 2 * hd; i += kConsumers)
+          (i < hd ? qn_s : kn_s - hd)[i] = i < hd ? L.qn_w[i] : L.kn_w[i - hd];
+    }
     // ---------------- A: x = RMSNorm(h); qkv rows
     if (l == 0) {
-      // h = dequantised embedding row (quartz/quantize.py:78-80)
+      // h = dequantised embedding row (quartz/quantize.py:78-80); CTA 0 keeps
+      // it as the residual stream
       const int8_t* er = a.embed_q + tok * H;
       const float es = a.embed_s[tok];
+      if (b == 0)
+        for (int i = tid; i < H; i += kConsumers) a.h[i] = static_cast<float>(er[i]) * es;
       float ss = 0.f;
       for (int i = tid; i < H; i += kConsumers) {
         const float v = static_cast<float>(er[i]) * es;
         ss = fmaf(v, v, ss);
-        if (b == 0) a.h[i] = v;
       }
       ss = consumer_sum(ss, red, tid);
       const float r = 1.0f / sqrtf(ss / static_cast<float>(H) + a.eps);
-      const int64_t nch = H / 16;
-      for (int i = tid; i < H; i += kConsumers) {
-        const int c = i >> 4, j = i & 15;
-        xs[((j >> 2) * nch + c) * 4 + (j & 3)] = static_cast<float>(er[i]) * es * r * L.in_w[i];
-      }
+      const int nch4 = H / 4;
+#pragma unroll
+      for (int j4 = 0; j4 < 4; ++j4)
+        for (int rem = tid; rem < nch4; rem += kConsumers) {
+          const int i = staged_src(j4, rem);
+          xs[j4 * nch4 + rem] = static_cast<float>(er[i]) * es * r * L.in_w[i];
+        }
     } else {
       stage_rmsnorm(xs, a.h, L.in_w, H, a.eps, red, tid);
     }
     consumer_sync();
-    int64_t r0, r1;
     {
-      split_range(static_cast<int64_t>(nq + 2 * nkv) * hd, P, b, r0, r1);
-      const Seg sg{nullptr, r1 - r0, H};
+      const Seg sg{nullptr, nA, H};
       const int rpc = sg.rows_per_chunk();
       for (int64_t c = 0; c < sg.chunks() && ok; ++c) {
         const uint8_t* slot = acquire();
         if (!slot) break;
         const int rows = static_cast<int>(min64(rpc, sg.rows - c * rpc));
-        for (int r = warp; r < rows; r += kConsumerWarps) {
-          const float d = row_dot(slot + r * H, reinterpret_cast<const uint8_t*>(xs), H, lane);
-          const int64_t row = r0 + c * rpc + r;
-          if (lane == 0) a.qkv[row] = d * __ldg(L.qkv_s + row);
-        }
+        float* out = a.qkv + a0 + c * rpc;
+        const float* sc_ = sA + c * rpc;
+        chunk_rows(slot, rows, H, xs, warp, lane, [&](int r, float d) { out[r] = d * sc_[r]; });
         release();
       }
     }
+    stamp(1 + 10 * l + 0);
     if (!ok || !consumer_grid_barrier(gbar, s_flag, tid, 0x310u + l)) { ok = false; break; }
+    stamp(2 + 10 * l + 0);
 
     // ---------------- B: attention items
     {
       const int64_t items = static_cast<int64_t>(nkv) * ap.S;
+      const float* qn = L.qn_w ? qn_s : nullptr;
+      const float* kn = L.qn_w ? kn_s : nullptr;
       for (int64_t it = b; it < items && ok; it += P) {
         const int g = static_cast<int>(it % nkv);
         const int64_t ci = it / nkv;
@@ -458,7 +595,7 @@ __global__ void __maxnreg__(224) decode_layers_kernel(const StepArgs a) {
           const float* src = a.qkv + static_cast<int64_t>(g * NR + r) * hd + lane * E;
 #pragma unroll
           for (int e = 0; e < E; ++e) x[e] = __ldcg(src + e);
-          dec::norm_rope<E>(x, L.qn_w, a.inv_freq, ap.pos, a.eps, lane);
+          dec::norm_rope<E>(x, qn, invf, ap.pos, a.eps, lane);
 #pragma unroll
           for (int e = 0; e < E; ++e) qs[r * hd + lane * E + e] = x[e];
         }
@@ -468,7 +605,7 @@ __global__ void __maxnreg__(224) decode_layers_kernel(const StepArgs a) {
           const float* vs = a.qkv + static_cast<int64_t>(nq + nkv + g) * hd + lane * E;
 #pragma unroll
           for (int e = 0; e < E; ++e) { k[e] = __ldcg(ks + e); v[e] = __ldcg(vs + e); }
-          dec::norm_rope<E>(k, L.kn_w, a.inv_freq, ap.pos, a.eps, lane);
+          dec::norm_rope<E>(k, kn, invf, ap.pos, a.eps, lane);
           float* kd = L.kc + (static_cast<int64_t>(g) * a.max_ctx + ap.pos) * hd + lane * E;
           float* vd = L.vc + (static_cast<int64_t>(g) * a.max_ctx + ap.pos) * hd + lane * E;
 #pragma unroll
@@ -480,19 +617,41 @@ __global__ void __maxnreg__(224) decode_layers_kernel(const StepArgs a) {
           }
         }
         consumer_sync();
-        // K chunk: scores sc[r][t] = (q_r . k_t) * scale
+        // K chunk: scores sc[r][t] = (q_r . k_t) * scale. Warp w holds rows
+        // w + 8k (k < KP) and reduces their KP dot products together.
         const uint8_t* kslot = acquire();
         if (!kslot) break;
-        const float* krows = reinterpret_cast<const float*>(kslot);
-        for (int t = warp; t < nt; t += kConsumerWarps) {
-          const bool fresh = owner && t0 + t == ap.pos;
-          const float* kr = fresh ? kvn : krows + t * hd;
-          for (int r = 0; r < NR; ++r) {
-            float d = 0.f;
+        {
+          const float* krows = reinterpret_cast<const float*>(kslot);
+          float kr[KP][E];
 #pragma unroll
-            for (int e = 0; e < E; ++e) d = fmaf(qs[r * hd + lane * E + e], kr[lane * E + e], d);
-            d = dec::warp_sum_f(d);
-            if (lane == 0) sc[r * 64 + t] = d * a.scale;
+          for (int k = 0; k < KP; ++k) {
+            const int t = warp + kConsumerWarps * k;
+            const bool fresh = owner && t0 + t == ap.pos;
+            const float* src = fresh ? kvn : krows + t * hd;
+#pragma unroll
+            for (int e = 0; e < E; ++e) kr[k][e] = t < nt ? src[lane * E + e] : 0.f;
+          }
+          for (int r = 0; r < NR; ++r) {
+            float qv[E], d[KP];
+#pragma unroll
+            for (int e = 0; e < E; ++e) qv[e] = qs[r * hd + lane * E + e];
+#pragma unroll
+            for (int k = 0; k < KP; ++k) {
+              d[k] = 0.f;
+#pragma unroll
+              for (int e = 0; e < E; ++e) d[k] = fmaf(qv[e], kr[k][e], d[k]);
+            }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+              for (int k = 0; k < KP; ++k) d[k] += __shfl_xor_sync(0xffffffffu, d[k], o);
+            if (lane == 0)
+#pragma unroll
+              for (int k = 0; k < KP; ++k) {
+                const int t = warp + kConsumerWarps * k;
+                if (t < nt) sc[r * 64 + t] = d[k] * a.scale;
+              }
           }
         }
         release();
@@ -517,12 +676,13 @@ __global__ void __maxnreg__(224) decode_layers_kernel(const StepArgs a) {
         if (!vslot) break;
         const float* vrows = reinterpret_cast<const float*>(vslot);
         float* pbase = a.part + (static_cast<int64_t>(g) * ap.S + ci) * NR * (hd + 2);
+        const int tf = owner ? static_cast<int>(ap.pos - t0) : -1;
         for (int i = tid; i < NR * hd; i += kConsumers) {
           const int r = i / hd, d = i - r * hd;
           float acc = 0.f;
+#pragma unroll 8
           for (int t = 0; t < nt; ++t) {
-            const bool fresh = owner && t0 + t == ap.pos;
-            const float v = fresh ? kvn[hd + d] : vrows[t * hd + d];
+            const float v = t == tf ? kvn[hd + d] : vrows[t * hd + d];
             acc = fmaf(sc[r * 64 + t], v, acc);
           }
           pbase[r * (hd + 2) + d] = acc;
@@ -538,90 +698,95 @@ __global__ void __maxnreg__(224) decode_layers_kernel(const StepArgs a) {
         consumer_sync();
         if (*s_last) {
           __threadfence();
-            merge_group<HD>(a.part + static_cast<int64_t>(g) * ap.S * NR * (hd + 2), ap.S, NR,
+          merge_group<HD>(a.part + static_cast<int64_t>(g) * ap.S * NR * (hd + 2), ap.S, NR,
                           a.attn + static_cast<int64_t>(g) * NR * hd, xs, tid);
           if (tid == 0) a.tickets[g] = 0u;
         }
         consumer_sync();
       }
     }
+    stamp(1 + 10 * l + 2);
     if (!ok || !consumer_grid_barrier(gbar, s_flag, tid, 0x320u + l)) { ok = false; break; }
+    stamp(2 + 10 * l + 2);
 
     // ---------------- C: h2 = h + Wo attn
-    stage_x<true>(xs, a.attn, Ko, tid, kConsumers);
+    stage_act(xs, a.attn, Ko, tid);
     consumer_sync();
     {
-      split_range(H, P, b, r0, r1);
-      const Seg sg{nullptr, r1 - r0, Ko};
+      const Seg sg{nullptr, nC, Ko};
       const int rpc = sg.rows_per_chunk();
       for (int64_t c = 0; c < sg.chunks() && ok; ++c) {
         const uint8_t* slot = acquire();
         if (!slot) break;
         const int rows = static_cast<int>(min64(rpc, sg.rows - c * rpc));
-        for (int r = warp; r < rows; r += kConsumerWarps) {
-          const float d = row_dot(slot + r * Ko, reinterpret_cast<const uint8_t*>(xs), Ko, lane);
-          const int64_t row = r0 + c * rpc + r;
-          if (lane == 0) a.h2[row] = d * __ldg(L.o_s + row) + __ldcg(a.h + row);
-        }
+        float* out = a.h2 + c0 + c * rpc;
+        const float* sc_ = sC + c * rpc;
+        const float* res = rC + c * rpc;
+        chunk_rows(slot, rows, Ko, xs, warp, lane,
+                   [&](int r, float d) { out[r] = d * sc_[r] + res[r]; });
         release();
       }
     }
+    stamp(1 + 10 * l + 4);
     if (!ok || !consumer_grid_barrier(gbar, s_flag, tid, 0x330u + l)) { ok = false; break; }
+    stamp(2 + 10 * l + 4);
 
     // ---------------- D: x = RMSNorm(h2); a = silu(gate x) * (up x)
+    for (int i = tid; i < nC; i += kConsumers) rE[i] = __ldcg(a.h2 + c0 + i);   // residual of E
     stage_rmsnorm(xs, a.h2, L.post_w, H, a.eps, red, tid);
     consumer_sync();
     {
-      split_range(I, P, b, r0, r1);
       for (int half = 0; half < 2 && ok; ++half) {
-        const Seg sg{nullptr, r1 - r0, H};
+        const Seg sg{nullptr, nD, H};
         const int rpc = sg.rows_per_chunk();
         for (int64_t c = 0; c < sg.chunks() && ok; ++c) {
           const uint8_t* slot = acquire();
           if (!slot) break;
           const int rows = static_cast<int>(min64(rpc, sg.rows - c * rpc));
-          for (int r = warp; r < rows; r += kConsumerWarps) {
-            const float d = row_dot(slot + r * H, reinterpret_cast<const uint8_t*>(xs), H, lane);
-            const int64_t u = c * rpc + r;   // unit index within this CTA
-            if (lane == 0) {
-              if (half == 0) {
-                gbuf[u] = d * __ldg(L.gu_s + r0 + u);
-              } else {
-                const float gv = gbuf[u];
-                const float uv = d * __ldg(L.gu_s + I + r0 + u);
-                // silu with the unclipped exponent, as the fused decode MLP
-                // (quartz/kernels/fused.py:40-54)
-                a.act[r0 + u] = gv / (1.0f + expf(-gv)) * uv;
-              }
-            }
+          const int u0 = static_cast<int>(c * rpc);   // unit index within this CTA
+          if (half == 0) {
+            chunk_rows(slot, rows, H, xs, warp, lane,
+                       [&](int r, float d) { gbuf[u0 + r] = d * sG[u0 + r]; });
+          } else {
+            float* out = a.act + d0 + u0;
+            chunk_rows(slot, rows, H, xs, warp, lane, [&](int r, float d) {
+              const float gv = gbuf[u0 + r];
+              const float uv = d * sU[u0 + r];
+              // silu with the unclipped exponent, as the fused decode MLP
+              // (quartz/kernels/fused.py:40-54)
+              out[r] = gv / (1.0f + expf(-gv)) * uv;
+            });
           }
           release();
         }
         consumer_sync();   // gate values visible before the up half reads them
       }
     }
+    stamp(1 + 10 * l + 6);
     if (!ok || !consumer_grid_barrier(gbar, s_flag, tid, 0x340u + l)) { ok = false; break; }
+    stamp(2 + 10 * l + 6);
 
     // ---------------- E: h = h2 + Wdown a
-    stage_x<true>(xs, a.act, I, tid, kConsumers);
+    stage_act(xs, a.act, I, tid);
     consumer_sync();
     {
-      split_range(H, P, b, r0, r1);
-      const Seg sg{nullptr, r1 - r0, I};
+      const Seg sg{nullptr, nC, I};
       const int rpc = sg.rows_per_chunk();
       for (int64_t c = 0; c < sg.chunks() && ok; ++c) {
         const uint8_t* slot = acquire();
         if (!slot) break;
         const int rows = static_cast<int>(min64(rpc, sg.rows - c * rpc));
-        for (int r = warp; r < rows; r += kConsumerWarps) {
-          const float d = row_dot(slot + r * I, reinterpret_cast<const uint8_t*>(xs), I, lane);
-          const int64_t row = r0 + c * rpc + r;
-          if (lane == 0) a.h[row] = d * __ldg(L.down_s + row) + __ldcg(a.h2 + row);
-        }
+        float* out = a.h + c0 + c * rpc;
+        const float* sc_ = sE + c * rpc;
+        const float* res = rE + c * rpc;
+        chunk_rows(slot, rows, I, xs, warp, lane,
+                   [&](int r, float d) { out[r] = d * sc_[r] + res[r]; });
         release();
       }
     }
+    stamp(1 + 10 * l + 8);
     if (!ok || !consumer_grid_barrier(gbar, s_flag, tid, 0x350u + l)) { ok = false; break; }
+    stamp(2 + 10 * l + 8);
   }
   if (!ok) {
     *abort_flag = 1u;

@@ -163,6 +163,7 @@ class DecodeEngine:
             self.gemm_ws = torch.empty(need, dtype=torch.uint8, device=dev)
         self._graph = None
         self._graph_steps = 0
+        self.trace = None   # set to a device uint64 tensor to record phase stamps
         self.fused = bool(fused) and self._setup_fused()
 
     def _setup_fused(self) -> bool:
@@ -238,7 +239,7 @@ class DecodeEngine:
                                      S.vocab, p(self.tok), p(self.pos_dev), p(self.inv_freq),
                                      p(self.norm_w), xn, H, S.inter, nq, nkv, hd, self.max_ctx,
                                      S.eps, self.attn_scale, p(self.step_ws),
-                                     self.step_ws.numel(), st))
+                                     self.step_ws.numel(), qd._ptr(self.trace), st))
             chk(lib.qz_gemv_w8(p(self.lm_q), p(self.lm_s), self.lm_s.shape[1], xn,
                                p(self.logits), S.vocab, H, None, st))
             chk(lib.qz_argmax(p(self.logits), 1, S.vocab, p(self.keys), p(self.tok),
