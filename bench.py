@@ -274,73 +274,87 @@ def run_decode(args, dev, world: int = 1) -> dict:
     (embedding, 28 layers, lm_head, argmax) replayed from CUDA graphs of 16
     tokens. Weights are the seeded synthetic checkpoint (0.598 GB of int8
     weights and scales per token, > L2); the tokens must equal the ones quartz
-    produced on the same checkpoint before anything is timed."""
+    produced on the same checkpoint before anything is timed. Two device
+    paths are timed: per-op launches (the engine's default, the headline) and
+    the one-launch persistent decode-layers kernel."""
     import torch
     from quartz_b200 import device as qdev
     from quartz_b200.decode import DecodeEngine
     from quartz_b200.model import QWEN3_0P6B, norm_weights, random_int8_weights, seeded_kv
 
     spec = QWEN3_0P6B
-    eng = DecodeEngine(spec, random_int8_weights(spec), norm_weights(spec),
-                       max_ctx=DECODE_KV + DECODE_TOKENS, max_prefill=1, device=dev)
-    eng.load_kv(seeded_kv(spec, DECODE_KV))
+    weights = list(random_int8_weights(spec))
+    kv = list(seeded_kv(spec, DECODE_KV))
     with np.load(REPO / "tests" / "golden" / "golden_model.npz") as z:
         gold = z["qwen3_0p6b_kv512__tokens"].tolist()
-    toks = eng.generate(DECODE_FIRST, DECODE_TOKENS, graph=True, unroll=DECODE_UNROLL)
-    if toks != gold:
-        bad = next(i for i, (a, b) in enumerate(zip(toks, gold)) if a != b)
-        raise SystemExit(f"decode parity failed at token {bad}: {toks[bad]} != {gold[bad]}")
     stream = torch.cuda.current_stream()
     nrep = DECODE_TOKENS // DECODE_UNROLL
-
-    def one_pass():
-        eng.reset(DECODE_KV)
-        eng.tok.fill_(DECODE_FIRST)
-        for _ in range(nrep):
-            eng.replay()
-
-    for _ in range(2):
-        one_pass()
-    torch.cuda.synchronize()
     passes = max(3, min(20, args.steps // 200))
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    _barrier(world)
-    e0.record(stream)
-    for _ in range(passes):
-        one_pass()
-    e1.record(stream)
-    _barrier(world)
-    qdev.check_status(dev)
-    ms_tok = _dist_max(e0.elapsed_time(e1) / (passes * DECODE_TOKENS), world)
-    # e2e through generate(): first token in from the host, the token list out
-    t0 = time.perf_counter()
-    for _ in range(passes):
-        eng.reset(DECODE_KV)
-        eng.generate(DECODE_FIRST, DECODE_TOKENS, graph=True, unroll=DECODE_UNROLL)
-    e2e_ms = _dist_max((time.perf_counter() - t0) * 1e3 / (passes * DECODE_TOKENS), world)
+
+    def measure(persistent: bool):
+        eng = DecodeEngine(spec, weights, norm_weights(spec), max_ctx=DECODE_KV + DECODE_TOKENS,
+                           max_prefill=1, device=dev, persistent=persistent)
+        eng.load_kv(kv)
+        toks = eng.generate(DECODE_FIRST, DECODE_TOKENS, graph=True, unroll=DECODE_UNROLL)
+        if toks != gold:
+            bad = next(i for i, (x, y) in enumerate(zip(toks, gold)) if x != y)
+            raise SystemExit(f"decode parity failed at token {bad}: {toks[bad]} != {gold[bad]}")
+
+        def one_pass():
+            eng.reset(DECODE_KV)
+            eng.tok.fill_(DECODE_FIRST)
+            for _ in range(nrep):
+                eng.replay()
+
+        for _ in range(2):
+            one_pass()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        _barrier(world)
+        e0.record(stream)
+        for _ in range(passes):
+            one_pass()
+        e1.record(stream)
+        _barrier(world)
+        qdev.check_status(dev)
+        ms_tok = _dist_max(e0.elapsed_time(e1) / (passes * DECODE_TOKENS), world)
+        # e2e through generate(): first token in from the host, the token list out
+        t0 = time.perf_counter()
+        for _ in range(passes):
+            eng.reset(DECODE_KV)
+            eng.generate(DECODE_FIRST, DECODE_TOKENS, graph=True, unroll=DECODE_UNROLL)
+        e2e_ms = _dist_max((time.perf_counter() - t0) * 1e3 / (passes * DECODE_TOKENS), world)
+        launches = eng._launches_per_token()
+        del eng
+        torch.cuda.empty_cache()
+        return ms_tok, e2e_ms, launches
+
+    ms_tok, e2e_ms, launches = measure(False)
+    ms_p, _, launches_p = measure(True)
     wbytes = spec.int8_bytes_per_token()
     ctx_mean = DECODE_KV + (DECODE_TOKENS + 1) / 2
     kvbytes = spec.kv_bytes_per_token(int(round(ctx_mean)))
     peak, peak_kind = _peaks()
     achieved = (wbytes + kvbytes) / (ms_tok * 1e-3) / 1e9
-    out = {"workload": "qwen3-0.6b all-int8 greedy decode, 512 prefilled KV positions, "
-                       "128 tokens, CUDA-graph replay (16 tokens per graph)",
-           "value": round(world / (ms_tok * 1e-3), 1), "unit": "tok/s",
-           "us_per_token": round(ms_tok * 1e3, 2), "passes": passes,
-           "tokens_match_reference": True,
-           "bytes_per_token": {"int8_weights_and_scales": wbytes, "kv_cache_mean": kvbytes},
-           "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
-                        "unit": UNIT, "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                        "per": "one GPU"},
-           "e2e": {"value": round(world / (e2e_ms * 1e-3), 1), "unit": "tok/s",
-                   "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8 * DECODE_TOKENS,
-                   "note": "DecodeEngine.generate per 128-token pass (first token in, "
-                           "token list out)"},
-           "gpu_launches": passes * DECODE_TOKENS * eng._launches_per_token(),
-           "parallelism": "replicas (one sequence per GPU)" if world > 1 else "single GPU"}
-    del eng
-    return out
+    return {"workload": "qwen3-0.6b all-int8 greedy decode, 512 prefilled KV positions, "
+                        "128 tokens, CUDA-graph replay (16 tokens per graph)",
+            "value": round(world / (ms_tok * 1e-3), 1), "unit": "tok/s",
+            "us_per_token": round(ms_tok * 1e3, 2), "passes": passes,
+            "tokens_match_reference": True,
+            "bytes_per_token": {"int8_weights_and_scales": wbytes, "kv_cache_mean": kvbytes},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": UNIT, "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "per": "one GPU"},
+            "e2e": {"value": round(world / (e2e_ms * 1e-3), 1), "unit": "tok/s",
+                    "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8 * DECODE_TOKENS,
+                    "note": "DecodeEngine.generate per 128-token pass (first token in, "
+                            "token list out)"},
+            "persistent_kernel": {"value": round(world / (ms_p * 1e-3), 1), "unit": "tok/s",
+                                  "us_per_token": round(ms_p * 1e3, 2),
+                                  "launches_per_token": launches_p},
+            "gpu_launches": passes * DECODE_TOKENS * launches,
+            "parallelism": "replicas (one sequence per GPU)" if world > 1 else "single GPU"}
 
 
 def _log(rank: int, msg: str) -> None:

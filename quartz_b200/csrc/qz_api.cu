@@ -861,6 +861,43 @@ int check_step_shape(const DeviceInfo& d, int H, int I, int nq, int nkv, int hd,
   return QZ_OK;
 }
 
+template <int HD, int NR>
+int launch_prefill_t(const float* q, const float* kc, const float* vc, float* out, int64_t M,
+                     int nq, int nkv, int64_t max_ctx, int64_t pos0, float scale,
+                     cudaStream_t st) {
+  auto fn = qz::dec::attn_prefill_tiled_kernel<HD, NR>;
+  constexpr int smem = qz::dec::prefill_tiled_smem<HD>();
+  static std::once_flag once[kMaxDevices];
+  int dev = 0;
+  QZ_CUDA(cudaGetDevice(&dev));
+  cudaError_t ae = cudaSuccess;
+  std::call_once(once[dev], [&] {
+    ae = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  });
+  QZ_CUDA(ae);
+  constexpr int BM = qz::dec::kPfThreads / (HD / qz::dec::kPfDims) / NR;
+  const dim3 grid(static_cast<unsigned>(qz::cdiv(M, BM)), static_cast<unsigned>(nkv));
+  fn<<<grid, qz::dec::kPfThreads, smem, st>>>(q, kc, vc, out, M, nq, max_ctx, pos0, scale);
+  QZ_CUDA(cudaGetLastError());
+  return QZ_OK;
+}
+
+// The tiled prefill attention for head_dim 64 / 128 and 1, 2, 4 or 8 query
+// heads per kv head; *done = false for other shapes.
+int launch_prefill_tiled(int hd, int n_rep, const float* q, const float* kc, const float* vc,
+                         float* out, int64_t M, int nq, int nkv, int64_t max_ctx, int64_t pos0,
+                         float scale, cudaStream_t st, bool* done) {
+  *done = true;
+#define QZ_PF_CASE(HD_, NR_) \
+  if (hd == (HD_) && n_rep == (NR_)) \
+    return launch_prefill_t<HD_, NR_>(q, kc, vc, out, M, nq, nkv, max_ctx, pos0, scale, st);
+  QZ_PF_CASE(64, 1) QZ_PF_CASE(64, 2) QZ_PF_CASE(64, 4) QZ_PF_CASE(64, 8)
+  QZ_PF_CASE(128, 1) QZ_PF_CASE(128, 2) QZ_PF_CASE(128, 4) QZ_PF_CASE(128, 8)
+#undef QZ_PF_CASE
+  *done = false;
+  return QZ_OK;
+}
+
 template <int E>
 int launch_step(const DeviceInfo& d, const qz::mk::StepArgs& a, cudaStream_t st) {
   auto fn = qz::mk::decode_layers_kernel<E>;
@@ -965,10 +1002,18 @@ int qz_attention_prefill(const float* q, const float* k_cache, const float* v_ca
     return fail(QZ_ERR_INVALID, "qz_attention_prefill: positions beyond the cache");
   if (M == 0) return QZ_OK;
   if (!q || !k_cache || !v_cache || !out) return fail(QZ_ERR_INVALID, "qz_attention_prefill: null pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (aligned16(q) && aligned16(k_cache) && aligned16(v_cache) && aligned16(out)) {
+    bool done = false;
+    if (int rc = launch_prefill_tiled(hd, nq / nkv, q, k_cache, v_cache, out, M, nq, nkv, max_ctx,
+                                      pos0, scale, st, &done))
+      return rc;
+    if (done) return QZ_OK;
+  }
   const int64_t warps = M * nq;
   const unsigned blocks = static_cast<unsigned>(qz::cdiv(warps * 32, 256));
-  qz::dec::attn_prefill_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      q, k_cache, v_cache, out, M, nq, nkv, hd, max_ctx, pos0, scale);
+  qz::dec::attn_prefill_kernel<<<blocks, 256, 0, st>>>(q, k_cache, v_cache, out, M, nq, nkv, hd,
+                                                       max_ctx, pos0, scale);
   QZ_CUDA(cudaGetLastError());
   return QZ_OK;
 }

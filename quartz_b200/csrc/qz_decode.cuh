@@ -18,6 +18,7 @@
 #pragma once
 
 #include "qz_device.cuh"
+#include "qz_stream.cuh"
 
 namespace qz {
 namespace dec {
@@ -209,6 +210,144 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, float* __res
     out[static_cast<int64_t>(h) * hd + d] = num / den;
   }
 }
+
+// Tiled causal prefill attention (fp32 on the CUDA cores, like the reference's
+// numpy attention). CTA (row block, kv head g) owns BM query rows of the NR
+// query heads of g: 128 threads, TPQ = HD / 32 threads per (row, head) query,
+// each holding 32 of its dimensions in registers (q and the accumulator). Key
+// tiles of BN rows of K and V are double-buffered in shared memory with
+// cp.async and read as broadcasts; per tile a thread computes its BN scores
+// (four keys at a time, so four dot products are in flight), rescales its
+// running accumulator once by e^(m_old - m_new), then adds e^(s - m_new) v.
+// Keys after a query's own position get probability 0.
+constexpr int kPfThreads = 128;
+constexpr int kPfBN = 32;
+constexpr int kPfDims = 32;   // dimensions per thread
+
+template <int HD, int NR>
+__global__ void __launch_bounds__(kPfThreads) attn_prefill_tiled_kernel(
+    const float* __restrict__ q, const float* __restrict__ kc, const float* __restrict__ vc,
+    float* __restrict__ out, int64_t M, int nq, int64_t max_ctx, int64_t pos0, float scale) {
+  constexpr int DP = kPfDims;
+  constexpr int TPQ = HD / DP;
+  constexpr int QPC = kPfThreads / TPQ;
+  constexpr int BM = QPC / NR;
+  constexpr int BN = kPfBN;
+  constexpr int TILE = BN * HD;                 // floats per K (or V) tile
+  extern __shared__ float4 pf_smem4[];
+  float* sm = reinterpret_cast<float*>(pf_smem4);   // [2 stages][K tile | V tile]
+  const int g = blockIdx.y;
+  const int tid = threadIdx.x;
+  const int qi = tid / TPQ, part = tid % TPQ;
+  const int rr = qi / BM, i = qi % BM;          // head within the group, row within the block
+  const int64_t row = static_cast<int64_t>(blockIdx.x) * BM + i;
+  const bool valid = row < M;
+  const int h = g * NR + rr;
+  const int64_t p = pos0 + (valid ? row : 0);   // this query's position
+  const int64_t last_row = min64(M, static_cast<int64_t>(blockIdx.x + 1) * BM) - 1;
+  const int64_t t_end = pos0 + last_row + 1;    // keys this CTA needs: [0, t_end)
+  const float* kg = kc + static_cast<int64_t>(g) * max_ctx * HD;
+  const float* vg = vc + static_cast<int64_t>(g) * max_ctx * HD;
+
+  float qv[DP], acc[DP];
+  {
+    const float* src = q + (static_cast<int64_t>(valid ? row : 0) * nq + h) * HD + part * DP;
+#pragma unroll
+    for (int d = 0; d < DP; d += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(src + d);
+      qv[d] = v.x; qv[d + 1] = v.y; qv[d + 2] = v.z; qv[d + 3] = v.w;
+    }
+  }
+#pragma unroll
+  for (int d = 0; d < DP; ++d) acc[d] = 0.f;
+  float m = -INFINITY, l = 0.f;
+
+  const int ntiles = static_cast<int>(cdiv(t_end, BN));
+  auto load_tile = [&](int tile, int stage) {
+    const int64_t t0 = static_cast<int64_t>(tile) * BN;
+    float* kd = sm + stage * 2 * TILE;
+    float* vd = kd + TILE;
+    for (int c = tid; c < TILE / 4; c += kPfThreads) {
+      const int j = c / (HD / 4);
+      const int64_t t = min64(t0 + j, t_end - 1);   // rows past t_end: any valid row (masked)
+      const int64_t off = t * HD + (c % (HD / 4)) * 4;
+      cp_async16(smem_u32(kd + c * 4), kg + off);
+      cp_async16(smem_u32(vd + c * 4), vg + off);
+    }
+    cp_async_commit();
+  };
+  load_tile(0, 0);
+  for (int tile = 0; tile < ntiles; ++tile) {
+    const int stage = tile & 1;
+    if (tile + 1 < ntiles) {
+      load_tile(tile + 1, stage ^ 1);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const float* ks = sm + stage * 2 * TILE + part * DP;
+    const float* vs = ks + TILE;
+    const int64_t t0 = static_cast<int64_t>(tile) * BN;
+    float sc[BN];
+    float mt = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < BN; j += 4) {
+      float dd[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int d = 0; d < DP; d += 4) {
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float4 k4 = *reinterpret_cast<const float4*>(ks + (j + u) * HD + d);
+          dd[u] = fmaf(qv[d], k4.x, dd[u]);
+          dd[u] = fmaf(qv[d + 1], k4.y, dd[u]);
+          dd[u] = fmaf(qv[d + 2], k4.z, dd[u]);
+          dd[u] = fmaf(qv[d + 3], k4.w, dd[u]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        float s = dd[u];
+#pragma unroll
+        for (int o = 1; o < TPQ; o <<= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+        s = t0 + j + u <= p ? s * scale : -INFINITY;
+        sc[j + u] = s;
+        mt = fmaxf(mt, s);
+      }
+    }
+    const float mn = fmaxf(m, mt);
+    const float corr = expf(m - mn);   // m = -inf on the first tile: corr = 0
+    l *= corr;
+#pragma unroll
+    for (int d = 0; d < DP; ++d) acc[d] *= corr;
+#pragma unroll
+    for (int j = 0; j < BN; ++j) {
+      const float pj = expf(sc[j] - mn);
+      l += pj;
+#pragma unroll
+      for (int d = 0; d < DP; d += 4) {
+        const float4 v4 = *reinterpret_cast<const float4*>(vs + j * HD + d);
+        acc[d] = fmaf(pj, v4.x, acc[d]);
+        acc[d + 1] = fmaf(pj, v4.y, acc[d + 1]);
+        acc[d + 2] = fmaf(pj, v4.z, acc[d + 2]);
+        acc[d + 3] = fmaf(pj, v4.w, acc[d + 3]);
+      }
+    }
+    m = mn;
+    __syncthreads();   // the stage is refilled two tiles later
+  }
+  if (valid) {
+    float* dst = out + (row * nq + h) * HD + part * DP;
+    const float inv = 1.0f / l;
+#pragma unroll
+    for (int d = 0; d < DP; d += 4)
+      *reinterpret_cast<float4*>(dst + d) =
+          make_float4(acc[d] * inv, acc[d + 1] * inv, acc[d + 2] * inv, acc[d + 3] * inv);
+  }
+}
+
+template <int HD>
+constexpr int prefill_tiled_smem() { return 2 * 2 * kPfBN * HD * 4; }
 
 // Prefill attention: query rows m (position pos0 + m) attend to cache positions
 // [0, pos0 + m] (causal). One warp per (row m, query head); online softmax

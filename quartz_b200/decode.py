@@ -57,7 +57,8 @@ class DecodeEngine:
     """
 
     def __init__(self, spec: ModelSpec, int8_weights: Mapping | Iterable, norms: Mapping,
-                 *, max_ctx: int, max_prefill: int = 512, device=None, fused: bool = True):
+                 *, max_ctx: int, max_prefill: int = 512, device=None,
+                 persistent: bool = False):
         self.spec = spec
         self.dev = torch.device("cuda", qd.ensure_device(device))
         dev = self.dev
@@ -164,11 +165,14 @@ class DecodeEngine:
         self._graph = None
         self._graph_steps = 0
         self.trace = None   # set to a device uint64 tensor to record phase stamps
-        self.fused = bool(fused) and self._setup_fused()
+        self.persistent = bool(persistent) and self._setup_persistent()
 
-    def _setup_fused(self) -> bool:
-        """Use the one-launch persistent kernel for all layers of a decode token
-        when the shapes allow it (per-row scales, head_dim 64/128/256, ...)."""
+    def _setup_persistent(self) -> bool:
+        """Use the one-launch persistent kernel (qz_decode_layers) for all layers
+        of a decode token when the shapes allow it (per-row scales, head_dim 64
+        or 128, ...). Measured on B200 it is parity-exact but not faster than the
+        per-op launches replayed from a CUDA graph (both latency-bound at about
+        35 us per Qwen3-0.6B layer), so it is opt-in."""
         S, lib = self.spec, self.lib
         per_row = all(t.shape[1] == 1 for L in self.layers
                       for t in (L.qkv_s, L.o_s, L.gu_s, L.down_s)) and self.embed_s.shape[1] == 1
@@ -234,7 +238,7 @@ class DecodeEngine:
         H, hd, nq, nkv = S.hidden, S.head_dim, S.n_heads, S.n_kv
         p = lambda t: t.data_ptr()  # noqa: E731
         h_a, h_b, xn = p(self.h_a), p(self.h_b), p(self.xn)
-        if self.fused:
+        if self.persistent:
             chk(lib.qz_decode_layers(p(self.layer_recs), S.layers, p(self.embed_q), p(self.embed_s),
                                      S.vocab, p(self.tok), p(self.pos_dev), p(self.inv_freq),
                                      p(self.norm_w), xn, H, S.inter, nq, nkv, hd, self.max_ctx,
@@ -270,7 +274,7 @@ class DecodeEngine:
                           1, st))
 
     def _launches_per_token(self) -> int:
-        if self.fused:
+        if self.persistent:
             return 4   # decode_layers, lm_head GEMV, argmax + finish
         # embed + per layer (rmsnorm, qkv, attention, o, rmsnorm, mlp) + norm, lm, argmax x2;
         # attention is one launch for the head shapes of the fused kernel

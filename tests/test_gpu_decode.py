@@ -178,7 +178,9 @@ def test_attention_decode_qkv(cuda_dev, qk_norm, nq, nkv, hd, pos, max_ctx):
 
 
 @pytest.mark.parametrize("nq,nkv,hd,M,pos0", [(4, 2, 16, 5, 0), (32, 8, 64, 130, 0),
-                                              (16, 8, 128, 9, 40), (8, 8, 256, 3, 7)])
+                                              (16, 8, 128, 9, 40), (8, 8, 256, 3, 7),
+                                              (16, 2, 128, 100, 300), (8, 8, 64, 33, 0),
+                                              (32, 8, 64, 512, 0), (8, 1, 128, 70, 5)])
 def test_attention_prefill(cuda_dev, nq, nkv, hd, M, pos0):
     from quartz_b200 import device as qd
     g = torch.Generator().manual_seed(M * 11 + hd)
@@ -221,14 +223,15 @@ def _golden(cid, key):
         return z[f"{cid}__{key}"]
 
 
-def _engine(case, extra_ctx=0, fused=True):
+def _engine(case, extra_ctx=0, persistent=False):
     from quartz_b200.decode import DecodeEngine
     from quartz_b200.model import ModelSpec, norm_weights, random_int8_weights
     spec = ModelSpec.from_hf(case["cfg"], case["arch"])
     start = case.get("kv_len") or len(case["prompt"])
     eng = DecodeEngine(spec, random_int8_weights(spec), norm_weights(spec),
                        max_ctx=start + case["steps"] + extra_ctx,
-                       max_prefill=max(2, len(case.get("prompt", [])) or 2), fused=fused)
+                       max_prefill=max(2, len(case.get("prompt", [])) or 2),
+                       persistent=persistent)
     return spec, eng
 
 
@@ -243,8 +246,8 @@ def _run(case, eng, graph, unroll=8):
 
 @pytest.mark.parametrize("cid", ["qwen3_tiny_prompt", "llama_tiny_prompt", "qwen3_tiny_kv",
                                  "qwen3_small_kv", "llama_small_prompt"])
-@pytest.mark.parametrize("fused", [True, False])
-def test_engine_small(cuda_dev, cid, fused):
+@pytest.mark.parametrize("persistent", [True, False])
+def test_engine_small(cuda_dev, cid, persistent):
     """Greedy tokens of small models, eager and graph replay; every eager step's
     top-8 logits against the reference's (1e-4 of the largest)."""
     from quartz_b200.model import seeded_kv
@@ -252,9 +255,9 @@ def test_engine_small(cuda_dev, cid, fused):
     gold = _golden(cid, "tokens").tolist()
     top_ids = _golden(cid, "top_ids")
     top_vals = _golden(cid, "top_vals")
-    _, eng = _engine(case, fused=fused)
-    if fused and case["cfg"]["head_dim"] in (64, 128):
-        assert eng.fused, "the one-launch decode kernel should take these shapes"
+    _, eng = _engine(case, persistent=persistent)
+    if persistent and case["cfg"]["head_dim"] in (64, 128):
+        assert eng.persistent, "the one-launch decode kernel should take these shapes"
     if case["start"] == "kv":
         eng.load_kv(seeded_kv(eng.spec, case["kv_len"]))
         tok = case["first"]
@@ -275,14 +278,14 @@ def test_engine_small(cuda_dev, cid, fused):
     assert _run(case, eng, graph=True, unroll=5) == gold, "graph"
 
 
-@pytest.mark.parametrize("fused", [True, False])
-def test_engine_qwen3_0p6b_kv512(cuda_dev, fused):
+@pytest.mark.parametrize("persistent", [True, False])
+def test_engine_qwen3_0p6b_kv512(cuda_dev, persistent):
     """The all-int8 Qwen3-0.6B decode workload: 512 prefilled positions, 128
     greedy tokens through the graph replay; the first step's top-8 logits too."""
     case = _cases()["qwen3_0p6b_kv512"]
     gold = _golden(case["id"], "tokens").tolist()
-    spec, eng = _engine(case, fused=fused)
-    assert eng.fused == fused
+    spec, eng = _engine(case, persistent=persistent)
+    assert eng.persistent == persistent
     from quartz_b200.model import seeded_kv
     eng.load_kv(seeded_kv(spec, case["kv_len"]))
     first = eng.generate(case["first"], 1, graph=False)
@@ -295,10 +298,12 @@ def test_engine_qwen3_0p6b_kv512(cuda_dev, fused):
     assert toks == gold
 
 
-def test_engine_llama_1b_prompt512(cuda_dev):
+@pytest.mark.parametrize("persistent", [True, False])
+def test_engine_llama_1b_prompt512(cuda_dev, persistent):
     """Llama-3.2-1B shapes: a 512-token prefill (tensor-core int8 GEMM, causal
     attention, llama3 RoPE) then greedy decode."""
     case = _cases()["llama_1b_prompt512"]
     gold = _golden(case["id"], "tokens").tolist()
-    _, eng = _engine(case)
+    _, eng = _engine(case, persistent=persistent)
+    assert eng.persistent == persistent
     assert _run(case, eng, graph=True, unroll=16) == gold
