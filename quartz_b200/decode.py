@@ -31,7 +31,7 @@ import numpy as np
 import torch
 
 from . import _lib, device as qd
-from .model import ModelSpec, rope_inv_freq
+from .model import ARCHS, ModelSpec, rope_inv_freq
 
 
 def _dev_f32(a, dev) -> torch.Tensor:
@@ -45,6 +45,58 @@ def _dev_i8(a, dev) -> torch.Tensor:
 class _Layer:
     __slots__ = ("qkv_q", "qkv_s", "o_q", "o_s", "gu_q", "gu_s", "down_q", "down_s", "in_w",
                  "post_w", "qn_w", "kn_w")
+
+
+def quartz_checkpoint(net) -> tuple[ModelSpec, dict, dict]:
+    """(spec, int8 weights, norm weights) of a quartz model quantised by
+    ``quantize_model(net, QuantConfig(default="int8", ...))``
+    (quartz/quantize.py:134-169), read from its module tree by attribute
+    (quartz/models/common.py:17-78; no import of quartz): QuantizedLinear /
+    QuantizedEmbedding leaves give (q, scale); a FusedMLP (quantize.py:87-97)
+    gives its stacked gate|up rows back as gate and up; RMSNorm leaves give
+    their weights. Arrays are not copied."""
+    cfg = net.config
+    arch = type(net).__name__
+    if arch not in ARCHS:
+        arch = (tuple(getattr(cfg, "architectures", ()) or ()) + (None,))[0]
+    spec = ModelSpec(arch=arch, hidden=cfg.hidden_size, layers=cfg.num_hidden_layers,
+                     n_heads=cfg.num_attention_heads, n_kv=cfg.num_key_value_heads,
+                     head_dim=cfg.head_dim, inter=cfg.intermediate_size, vocab=cfg.vocab_size,
+                     rope_theta=float(cfg.rope_theta), tie=bool(cfg.tie_word_embeddings),
+                     rope_scaling=getattr(cfg, "rope_scaling", None),
+                     eps=float(getattr(cfg, "rms_norm_eps", 1e-6)))
+
+    def q8(leaf, name):
+        if not (hasattr(leaf, "q") and hasattr(leaf, "scale")):
+            raise ValueError(f"{name} is not int8-quantised (quantise with "
+                             f"QuantConfig(default='int8'))")
+        return np.asarray(leaf.q), np.asarray(leaf.scale)
+
+    m = net.model
+    int8 = {"model.embed_tokens": q8(m.embed_tokens, "model.embed_tokens")}
+    norms = {"model.norm": np.asarray(m.norm.weight)}
+    for i, layer in enumerate(m.layers):
+        p = f"model.layers.{i}."
+        att = layer.self_attn
+        for n in ("q_proj", "k_proj", "v_proj", "o_proj"):
+            int8[p + "self_attn." + n] = q8(getattr(att, n), p + "self_attn." + n)
+        mlp = layer.mlp
+        if hasattr(mlp, "gu_q"):
+            I = int(mlp.inter)
+            int8[p + "mlp.gate_proj"] = (np.asarray(mlp.gu_q)[:I], np.asarray(mlp.gu_s)[:I])
+            int8[p + "mlp.up_proj"] = (np.asarray(mlp.gu_q)[I:], np.asarray(mlp.gu_s)[I:])
+            int8[p + "mlp.down_proj"] = (np.asarray(mlp.down_q), np.asarray(mlp.down_s))
+        else:
+            for n in ("gate_proj", "up_proj", "down_proj"):
+                int8[p + "mlp." + n] = q8(getattr(mlp, n), p + "mlp." + n)
+        norms[p + "input_layernorm"] = np.asarray(layer.input_layernorm.weight)
+        norms[p + "post_attention_layernorm"] = np.asarray(layer.post_attention_layernorm.weight)
+        if spec.qk_norm:
+            norms[p + "self_attn.q_norm"] = np.asarray(att.q_norm.weight)
+            norms[p + "self_attn.k_norm"] = np.asarray(att.k_norm.weight)
+    if not spec.tie:
+        int8["lm_head"] = q8(net.lm_head, "lm_head")
+    return spec, int8, norms
 
 
 class DecodeEngine:
@@ -195,6 +247,13 @@ class DecodeEngine:
                 L.post_w, L.qn_w, L.kn_w, self.k_cache[li], self.v_cache[li])])
         self.layer_recs = torch.tensor(recs, dtype=torch.int64).to(self.dev)
         return True
+
+    @classmethod
+    def from_quartz(cls, net, **kw) -> "DecodeEngine":
+        """An engine on the int8 weights of a quantised quartz model (see
+        quartz_checkpoint); keyword arguments as the constructor's."""
+        spec, int8, norms = quartz_checkpoint(net)
+        return cls(spec, int8, norms, **kw)
 
     # ------------------------------------------------------------------ state
     def reset(self, pos: int = 0) -> None:

@@ -104,3 +104,54 @@ def test_seeded_kv_shapes():
     rng = np.random.default_rng(99)
     k0 = rng.standard_normal((1, spec.n_kv, 40, spec.head_dim), dtype=np.float32)
     assert np.array_equal(k, k0[0])
+
+
+def _quartz_like(spec, fused_mlp):
+    """An object tree shaped like a quantised quartz model
+    (quartz/models/common.py, quartz/quantize.py), built from the synthetic
+    checkpoint."""
+    from types import SimpleNamespace as NS
+    w = {n: (q, s) for n, q, s in random_int8_weights(spec)}
+    lin = lambda n: NS(q=w[n][0], scale=w[n][1], weight=w[n][0])  # noqa: E731
+    norm = lambda d: NS(weight=np.ones(d, np.float32))  # noqa: E731
+    layers = []
+    for i in range(spec.layers):
+        p = f"model.layers.{i}."
+        att = NS(q_proj=lin(p + "self_attn.q_proj"), k_proj=lin(p + "self_attn.k_proj"),
+                 v_proj=lin(p + "self_attn.v_proj"), o_proj=lin(p + "self_attn.o_proj"))
+        if spec.qk_norm:
+            att.q_norm, att.k_norm = norm(spec.head_dim), norm(spec.head_dim)
+        if fused_mlp:
+            g, u, d = (w[p + "mlp." + n] for n in ("gate_proj", "up_proj", "down_proj"))
+            mlp = NS(gu_q=np.concatenate([g[0], u[0]]), gu_s=np.concatenate([g[1], u[1]]),
+                     down_q=d[0], down_s=d[1], inter=spec.inter, hidden=spec.hidden)
+        else:
+            mlp = NS(gate_proj=lin(p + "mlp.gate_proj"), up_proj=lin(p + "mlp.up_proj"),
+                     down_proj=lin(p + "mlp.down_proj"))
+        layers.append(NS(self_attn=att, mlp=mlp, input_layernorm=norm(spec.hidden),
+                         post_attention_layernorm=norm(spec.hidden)))
+    cfg = NS(hidden_size=spec.hidden, num_hidden_layers=spec.layers,
+             num_attention_heads=spec.n_heads, num_key_value_heads=spec.n_kv,
+             head_dim=spec.head_dim, intermediate_size=spec.inter, vocab_size=spec.vocab,
+             rope_theta=spec.rope_theta, tie_word_embeddings=spec.tie,
+             rope_scaling=spec.rope_scaling, rms_norm_eps=spec.eps, architectures=())
+    net = type(spec.arch, (), {})()
+    net.config = cfg
+    net.model = NS(embed_tokens=lin("model.embed_tokens"), layers=layers, norm=norm(spec.hidden))
+    if not spec.tie:
+        net.lm_head = lin("lm_head")
+    return net, w
+
+
+@pytest.mark.parametrize("cid,fused", [("qwen3_tiny_kv", True), ("llama_tiny_prompt", False),
+                                       ("llama_small_prompt", True)])
+def test_quartz_checkpoint_reads_a_quartz_model(cid, fused):
+    from quartz_b200.decode import quartz_checkpoint
+    spec = _spec(cid)
+    net, w = _quartz_like(spec, fused)
+    got_spec, int8, norms = quartz_checkpoint(net)
+    assert got_spec == spec and got_spec.rope_scaling == spec.rope_scaling
+    assert set(int8) == set(w)
+    for n, (q, s) in w.items():
+        assert np.array_equal(int8[n][0], q) and np.array_equal(int8[n][1], s), n
+    assert set(norms) == set(norm_weights(spec))
