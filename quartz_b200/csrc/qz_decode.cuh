@@ -216,7 +216,8 @@ __global__ void attn_combine_kernel(const float* __restrict__ part, float* __res
 // query heads of g: 128 threads, TPQ = HD / 32 threads per (row, head) query,
 // each holding 32 of its dimensions in registers (q and the accumulator). Key
 // tiles of BN rows of K and V are double-buffered in shared memory with
-// cp.async and read as broadcasts; per tile a thread computes its BN scores
+// cp.async (the TPQ slices of a row interleaved float4 by float4, so a
+// query's threads hit distinct banks) and read as broadcasts; per tile a thread computes its BN scores
 // (four keys at a time, so four dot products are in flight), rescales its
 // running accumulator once by e^(m_old - m_new), then adds e^(s - m_new) v.
 // Keys after a query's own position get probability 0.
@@ -268,11 +269,14 @@ __global__ void __launch_bounds__(kPfThreads) attn_prefill_tiled_kernel(
     float* kd = sm + stage * 2 * TILE;
     float* vd = kd + TILE;
     for (int c = tid; c < TILE / 4; c += kPfThreads) {
-      const int j = c / (HD / 4);
+      const int j = c / (HD / 4), f = c % (HD / 4);   // row, float4 of the row
       const int64_t t = min64(t0 + j, t_end - 1);   // rows past t_end: any valid row (masked)
-      const int64_t off = t * HD + (c % (HD / 4)) * 4;
-      cp_async16(smem_u32(kd + c * 4), kg + off);
-      cp_async16(smem_u32(vd + c * 4), vg + off);
+      const int64_t off = t * HD + f * 4;
+      // float4 f = (slice f / (DP/4), chunk f % (DP/4)) goes to chunk * TPQ + slice, so the
+      // TPQ threads of a query read adjacent 16-byte words (distinct banks)
+      const int dst = j * HD + ((f % (DP / 4)) * TPQ + f / (DP / 4)) * 4;
+      cp_async16(smem_u32(kd + dst), kg + off);
+      cp_async16(smem_u32(vd + dst), vg + off);
     }
     cp_async_commit();
   };
@@ -286,7 +290,7 @@ __global__ void __launch_bounds__(kPfThreads) attn_prefill_tiled_kernel(
       cp_async_wait<0>();
     }
     __syncthreads();
-    const float* ks = sm + stage * 2 * TILE + part * DP;
+    const float* ks = sm + stage * 2 * TILE + part * 4;   // chunk c of this slice at c * TPQ * 4
     const float* vs = ks + TILE;
     const int64_t t0 = static_cast<int64_t>(tile) * BN;
     float sc[BN];
@@ -298,7 +302,7 @@ __global__ void __launch_bounds__(kPfThreads) attn_prefill_tiled_kernel(
       for (int d = 0; d < DP; d += 4) {
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-          const float4 k4 = *reinterpret_cast<const float4*>(ks + (j + u) * HD + d);
+          const float4 k4 = *reinterpret_cast<const float4*>(ks + (j + u) * HD + d * TPQ);
           dd[u] = fmaf(qv[d], k4.x, dd[u]);
           dd[u] = fmaf(qv[d + 1], k4.y, dd[u]);
           dd[u] = fmaf(qv[d + 2], k4.z, dd[u]);
@@ -326,7 +330,7 @@ __global__ void __launch_bounds__(kPfThreads) attn_prefill_tiled_kernel(
       l += pj;
 #pragma unroll
       for (int d = 0; d < DP; d += 4) {
-        const float4 v4 = *reinterpret_cast<const float4*>(vs + j * HD + d);
+        const float4 v4 = *reinterpret_cast<const float4*>(vs + j * HD + d * TPQ);
         acc[d] = fmaf(pj, v4.x, acc[d]);
         acc[d + 1] = fmaf(pj, v4.y, acc[d + 1]);
         acc[d + 2] = fmaf(pj, v4.z, acc[d + 2]);

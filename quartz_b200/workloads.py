@@ -92,3 +92,73 @@ def mlp_algorithmic_bytes(H, I, ng=1, ngd=1, M=1) -> int:
     """gate|up and down int8 + their scales + x in + out; the [I] intermediate
     stays on chip/L2 and is not counted."""
     return 2 * I * H + H * I + 4 * (2 * I * ng + H * ngd) + 4 * M * H * 2
+
+
+# ---------------------------------------------------------------------------
+# Command line: run ONE workload on cuda:0 and exit, so that a profiler can
+# capture exactly its launches.
+#
+#   python -m quartz_b200.workloads gemm M N K      tensor-core GEMM, 3 calls
+#   python -m quartz_b200.workloads mlp             28-layer fused MLP body, once
+#   python -m quartz_b200.workloads decode [--persistent] [--tokens T]
+#                                                   Qwen3-0.6B, 512 prefilled KV
+#                                                   positions, T eager tokens
+#   python -m quartz_b200.workloads prefill         Llama-3.2-1B 512-token prefill
+# ---------------------------------------------------------------------------
+def _main(argv=None) -> None:
+    import argparse
+
+    import torch
+
+    ap = argparse.ArgumentParser(prog="python -m quartz_b200.workloads")
+    sub = ap.add_subparsers(dest="what", required=True)
+    g = sub.add_parser("gemm")
+    g.add_argument("M", type=int)
+    g.add_argument("N", type=int)
+    g.add_argument("K", type=int)
+    sub.add_parser("mlp")
+    d = sub.add_parser("decode")
+    d.add_argument("--persistent", action="store_true")
+    d.add_argument("--tokens", type=int, default=3)
+    sub.add_parser("prefill")
+    a = ap.parse_args(argv)
+    dev = torch.device("cuda", 0)
+    from . import device as qd
+    qd.ensure_device(dev)
+    if a.what == "gemm":
+        c = gemv_case(a.N, a.K, M=a.M, seed=0)
+        q, s = torch.from_numpy(c.q).to(dev), torch.from_numpy(c.scale).to(dev)
+        X = torch.from_numpy(c.x).to(dev)
+        for _ in range(3):
+            Y = qd.gemm(q, s, X)
+        torch.cuda.synchronize()
+        print(f"gemm {a.M}x{a.N}x{a.K}: |Y|max {float(Y.abs().max()):.4g}")
+    elif a.what == "mlp":
+        for l in range(MLP_LAYERS):
+            m = mlp_case(MLP_H, MLP_I, seed=MLP_LAYER_SEED0 + l)
+            t = [torch.from_numpy(v).to(dev) for v in (m.gu_q, m.gu_s, m.x[0], m.down_q, m.down_s)]
+            out = qd.fused_mlp(*t)
+        torch.cuda.synchronize()
+        print(f"mlp body: |out|max {float(out.abs().max()):.4g}")
+    else:
+        from .decode import DecodeEngine
+        from .model import LLAMA_3P2_1B, QWEN3_0P6B, norm_weights, random_int8_weights, seeded_kv
+        if a.what == "decode":
+            spec = QWEN3_0P6B
+            eng = DecodeEngine(spec, random_int8_weights(spec), norm_weights(spec), max_ctx=640,
+                               max_prefill=1, device=dev, persistent=a.persistent)
+            eng.load_kv(seeded_kv(spec, 512))
+            toks = eng.generate(42, a.tokens, graph=False)
+            print(f"decode ({'persistent' if eng.persistent else 'per-op'}): {toks}")
+        else:
+            spec = LLAMA_3P2_1B
+            eng = DecodeEngine(spec, random_int8_weights(spec), norm_weights(spec), max_ctx=600,
+                               max_prefill=512, device=dev)
+            ids = np.random.default_rng(7).integers(0, spec.vocab, 512).tolist()
+            print(f"prefill: first token {eng.prefill(ids)}")
+        torch.cuda.synchronize()
+    qd.check_status(dev)
+
+
+if __name__ == "__main__":
+    _main()
