@@ -35,11 +35,22 @@ from .model import ARCHS, ModelSpec, rope_inv_freq
 
 
 def _dev_f32(a, dev) -> torch.Tensor:
+    if isinstance(a, torch.Tensor):
+        return a.to(device=dev, dtype=torch.float32).contiguous()
     return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(dev)
 
 
 def _dev_i8(a, dev) -> torch.Tensor:
+    if isinstance(a, torch.Tensor):
+        return a.to(device=dev, dtype=torch.int8).contiguous()
     return torch.from_numpy(np.ascontiguousarray(a, dtype=np.int8)).to(dev)
+
+
+def _cat(parts):
+    """Row concatenation of numpy arrays or torch tensors (not mixed)."""
+    if isinstance(parts[0], torch.Tensor):
+        return torch.cat(parts, 0)
+    return np.concatenate(parts, 0)
 
 
 class _Layer:
@@ -128,12 +139,12 @@ class DecodeEngine:
             L = self.layers[i]
             if len({w[n][1].shape[1] for n in ("q_proj", "k_proj", "v_proj")}) != 1:
                 raise ValueError("q/k/v scales must share a group count")
-            L.qkv_q = _dev_i8(np.concatenate([w[n][0] for n in ("q_proj", "k_proj", "v_proj")]), dev)
-            L.qkv_s = _dev_f32(np.concatenate([w[n][1] for n in ("q_proj", "k_proj", "v_proj")]), dev)
+            L.qkv_q = _dev_i8(_cat([w[n][0] for n in ("q_proj", "k_proj", "v_proj")]), dev)
+            L.qkv_s = _dev_f32(_cat([w[n][1] for n in ("q_proj", "k_proj", "v_proj")]), dev)
             L.o_q, L.o_s = _dev_i8(w["o_proj"][0], dev), _dev_f32(w["o_proj"][1], dev)
             # gate rows over up rows, the layout of quartz/quantize.py:95-96
-            L.gu_q = _dev_i8(np.concatenate([w["gate_proj"][0], w["up_proj"][0]]), dev)
-            L.gu_s = _dev_f32(np.concatenate([w["gate_proj"][1], w["up_proj"][1]]), dev)
+            L.gu_q = _dev_i8(_cat([w["gate_proj"][0], w["up_proj"][0]]), dev)
+            L.gu_s = _dev_f32(_cat([w["gate_proj"][1], w["up_proj"][1]]), dev)
             L.down_q, L.down_s = _dev_i8(w["down_proj"][0], dev), _dev_f32(w["down_proj"][1], dev)
 
         pairs = ((n, *qs) for n, qs in int8_weights.items()) \

@@ -155,3 +155,33 @@ def test_quartz_checkpoint_reads_a_quartz_model(cid, fused):
     for n, (q, s) in w.items():
         assert np.array_equal(int8[n][0], q) and np.array_equal(int8[n][1], s), n
     assert set(norms) == set(norm_weights(spec))
+
+
+@pytest.mark.parametrize("cid,world", [("llama_small_prompt", 2), ("qwen3_small_kv", 2),
+                                       ("qwen3_tiny_kv", 2)])
+def test_tp_shard_reassembles(cid, world):
+    """The ranks' parts of a checkpoint put back together give the full
+    matrices: q/k/v and gate/up rows, o and down columns, lm_head vocab rows."""
+    from quartz_b200.tp_decode import tp_shard
+    spec = _spec(cid)
+    w = {n: (q, s) for n, q, s in random_int8_weights(spec)}
+    parts = [tp_shard(spec, w, r, world) for r in range(world)]
+    assert all(p[0].n_heads * world == spec.n_heads and p[0].n_kv * world == spec.n_kv
+               and p[0].inter * world == spec.inter for p in parts)
+    for name, (q, s) in w.items():
+        leaf = name.rsplit(".", 1)[-1]
+        if name in ("model.embed_tokens",):
+            assert all(np.array_equal(p[1][name][0], q) for p in parts)
+        elif name == "lm_head":
+            continue
+        elif leaf in ("o_proj", "down_proj"):
+            assert np.array_equal(np.concatenate([p[1][name][0] for p in parts], 1), q), name
+            assert all(np.array_equal(p[1][name][1], s) for p in parts)
+        else:
+            assert np.array_equal(np.concatenate([p[1][name][0] for p in parts], 0), q), name
+            assert np.array_equal(np.concatenate([p[1][name][1] for p in parts], 0), s), name
+    lm = w["lm_head"] if "lm_head" in w else w["model.embed_tokens"]
+    assert np.array_equal(np.concatenate([p[2][0] for p in parts]), lm[0])
+    assert [p[2][2] for p in parts] == [0] + [p[2][3] for p in parts][:-1]
+    with pytest.raises(ValueError):
+        tp_shard(spec, w, 0, 3)
