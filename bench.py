@@ -449,7 +449,68 @@ def run_tp(args, rank: int, world: int, dev) -> dict:
         torch.cuda.synchronize()
     del layers, head
     torch.cuda.empty_cache()
+    out["decode"] = run_tp_decode(args, rank, world, dev)
     return out
+
+
+TP_CTX, TP_TOKENS, TP_UNROLL = 2048, 64, 16
+
+
+def run_tp_decode(args, rank: int, world: int, dev) -> dict:
+    """Greedy decode of one Qwen3-8B sequence split over the ranks
+    (TPDecodeEngine: head-sharded attention, unit-sharded MLP, vocab-sharded
+    lm_head, two all-reduces per layer), at context 2048..2112, 64 tokens per
+    pass replayed from CUDA graphs of 16. Weights are drawn on the device per
+    shard (timing does not depend on the values; the engine's tokens are
+    tested against the reference on smaller checkpoints)."""
+    import torch
+    from quartz_b200.model import QWEN3_8B, norm_weights
+    from quartz_b200.tp_decode import TPDecodeEngine, random_tp_shard
+    spec = QWEN3_8B
+    shard = random_tp_shard(spec, rank, world, dev)
+    eng = TPDecodeEngine(spec, None, norm_weights(spec), max_ctx=TP_CTX + TP_TOKENS,
+                         max_prefill=1, device=dev, presharded=shard)
+    del shard
+    stream = torch.cuda.current_stream()
+
+    def one_pass():
+        eng.reset(TP_CTX)
+        eng.tok.fill_(7)
+        for _ in range(TP_TOKENS // TP_UNROLL):
+            eng.replay()
+
+    eng.reset(TP_CTX)
+    eng.capture(TP_UNROLL)
+    for _ in range(2):
+        one_pass()
+    torch.cuda.synchronize()
+    passes = 3
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    _barrier(world)
+    e0.record(stream)
+    for _ in range(passes):
+        one_pass()
+    e1.record(stream)
+    _barrier(world)
+    ms_tok = _dist_max(e0.elapsed_time(e1) / (passes * TP_TOKENS), world)
+    eng._graph = None        # a graph holding NCCL calls goes before the process group
+    del eng
+    torch.cuda.empty_cache()
+    wbytes = spec.int8_bytes_per_token()
+    kvbytes = spec.kv_bytes_per_token(TP_CTX + TP_TOKENS // 2)
+    peak, peak_kind = _peaks()
+    per_gpu = (wbytes + kvbytes) / world
+    achieved = per_gpu / (ms_tok * 1e-3) / 1e9
+    return {"workload": "qwen3-8b all-int8 greedy decode, one sequence over the ranks, context "
+                        f"{TP_CTX}..{TP_CTX + TP_TOKENS}, CUDA-graph replay",
+            "value": round(1.0 / (ms_tok * 1e-3), 1), "unit": "tok/s",
+            "us_per_token": round(ms_tok * 1e3, 1), "n_gpus": world, "scaling": "strong",
+            "bytes_per_token": {"int8_weights_and_scales": wbytes, "kv_cache": kvbytes},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": UNIT, "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "per": "one GPU (its 1/N of the bytes)"},
+            "collectives_per_token": 2 * spec.layers + 1}
 
 
 def run_ours(args, rank: int, world: int, local: int) -> dict | None:

@@ -269,6 +269,38 @@ int qz_decode_layers(const qz_decoder_layer* layers, int n_layers, const int8_t*
                      float eps, float scale, void* ws, size_t ws_bytes, uint64_t* trace,
                      void* stream);
 
+/* ------------------------------------------------------------------------
+ * Peer-memory all-reduce for tensor-parallel decoding (one process per GPU,
+ * GPUs of one node with peer access over NVLink). quartz has no counterpart:
+ * it is single-process.
+ * ------------------------------------------------------------------------ */
+
+/* Bytes of one rank's communication buffer for `ranks` ranks and sums of at
+ * most n_max floats (n_max a multiple of 4). */
+int qz_comm_buffer_bytes(int ranks, int64_t n_max, int64_t* bytes);
+
+/* cudaMalloc + zero a communication buffer on the current device / free it.
+ * (Its own allocation, so that its IPC handle maps exactly this range.) */
+int qz_comm_alloc(int64_t bytes, void** ptr);
+int qz_comm_free(void* ptr);
+
+/* 64-byte CUDA IPC handle of a qz_comm_alloc buffer; open a peer's handle in
+ * this process (peer access enabled lazily); close it again. */
+int qz_ipc_handle(const void* ptr, void* handle64);
+int qz_ipc_open(const void* handle64, void** ptr);
+int qz_ipc_close(void* ptr);
+
+/*
+ * out[i] = sum over ranks of their in[i], i < n, identical on every rank (the
+ * sum runs in rank order). peer_buffers: host array of the `ranks` buffers as
+ * mapped in this process (this rank's own at [rank]). Every rank must make
+ * the same sequence of calls on its buffer; a call waits for its peers' pushes
+ * for at most about a second (then the status word records it). in may equal
+ * out. n a multiple of 4, in/out 16-byte aligned.
+ */
+int qz_allreduce_sum(const float* in, float* out, int64_t n, int64_t n_max,
+                     void* const* peer_buffers, int rank, int ranks, void* stream);
+
 /* Read the device status word of the current device into words[0..3]
  * ({error bits, first error site, block of first error, error count}); when
  * clear != 0 reset it to zero afterwards. Synchronises the device. */

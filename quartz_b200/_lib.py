@@ -52,6 +52,13 @@ SIGNATURES = {
     "qz_decode_step_workspace_bytes": ([_int, _int, _int, _int, _int, _i64, ctypes.POINTER(_i64)],
                                        _int),
     "qz_decode_layers_supported": ([_int, _int, _int, _int, _int, _i64], _int),
+    "qz_comm_buffer_bytes": ([_int, _i64, ctypes.POINTER(_i64)], _int),
+    "qz_comm_alloc": ([_i64, ctypes.POINTER(_vp)], _int),
+    "qz_comm_free": ([_vp], _int),
+    "qz_ipc_handle": ([_vp, _vp], _int),
+    "qz_ipc_open": ([_vp, ctypes.POINTER(_vp)], _int),
+    "qz_ipc_close": ([_vp], _int),
+    "qz_allreduce_sum": ([_vp, _vp, _i64, _i64, _vp, _int, _int, _vp], _int),
     "qz_decode_layers": ([_vp, _int, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _int, _int, _int,
                           _int, _int, _i64, ctypes.c_float, ctypes.c_float, _vp, ctypes.c_size_t,
                           _vp, _vp], _int),

@@ -15,6 +15,7 @@
 #include "qz_tc_gemm.cuh"
 #include "qz_decode.cuh"
 #include "qz_decode_step.cuh"
+#include "qz_comm.cuh"
 
 namespace {
 
@@ -992,6 +993,82 @@ int qz_decode_layers(const qz_decoder_layer* layers, int n_layers, const int8_t*
   a.trace = reinterpret_cast<unsigned long long*>(trace);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   return hd == 64 ? launch_step<2>(*d, a, st) : launch_step<4>(*d, a, st);
+}
+
+// ---------------------------------------------------------------------------
+// peer-memory all-reduce for tensor-parallel decoding
+// ---------------------------------------------------------------------------
+static_assert(sizeof(cudaIpcMemHandle_t) == 64, "CUDA IPC handles are 64 bytes");
+
+int qz_comm_buffer_bytes(int ranks, int64_t n_max, int64_t* bytes) {
+  if (!bytes || ranks < 1 || ranks > qz::comm::kMaxRanks || n_max < 4 || n_max % 4)
+    return fail(QZ_ERR_INVALID, "qz_comm_buffer_bytes: 1..8 ranks and n_max a positive multiple of 4");
+  *bytes = qz::comm::buffer_bytes(ranks, n_max);
+  return QZ_OK;
+}
+
+int qz_comm_alloc(int64_t bytes, void** ptr) {
+  if (!ptr || bytes <= 0) return fail(QZ_ERR_INVALID, "qz_comm_alloc: bad arguments");
+  void* p = nullptr;
+  QZ_CUDA(cudaMalloc(&p, static_cast<size_t>(bytes)));
+  const cudaError_t e = cudaMemset(p, 0, static_cast<size_t>(bytes));
+  if (e != cudaSuccess) {
+    cudaFree(p);
+    return fail(QZ_ERR_CUDA, std::string("qz_comm_alloc: cudaMemset: ") + cudaGetErrorString(e));
+  }
+  *ptr = p;
+  return QZ_OK;
+}
+
+int qz_comm_free(void* ptr) {
+  if (ptr) QZ_CUDA(cudaFree(ptr));
+  return QZ_OK;
+}
+
+int qz_ipc_handle(const void* ptr, void* handle64) {
+  if (!ptr || !handle64) return fail(QZ_ERR_INVALID, "qz_ipc_handle: null pointer");
+  cudaIpcMemHandle_t h;
+  QZ_CUDA(cudaIpcGetMemHandle(&h, const_cast<void*>(ptr)));
+  std::memcpy(handle64, &h, sizeof(h));
+  return QZ_OK;
+}
+
+int qz_ipc_open(const void* handle64, void** ptr) {
+  if (!handle64 || !ptr) return fail(QZ_ERR_INVALID, "qz_ipc_open: null pointer");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle64, sizeof(h));
+  QZ_CUDA(cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess));
+  return QZ_OK;
+}
+
+int qz_ipc_close(void* ptr) {
+  if (ptr) QZ_CUDA(cudaIpcCloseMemHandle(ptr));
+  return QZ_OK;
+}
+
+int qz_allreduce_sum(const float* in, float* out, int64_t n, int64_t n_max,
+                     void* const* peer_buffers, int rank, int ranks, void* stream) {
+  if (ranks < 1 || ranks > qz::comm::kMaxRanks || rank < 0 || rank >= ranks)
+    return fail(QZ_ERR_INVALID, "qz_allreduce_sum: bad rank / rank count");
+  if (n < 0 || n > n_max || n % 4 || n_max % 4)
+    return fail(QZ_ERR_INVALID, "qz_allreduce_sum: n must be a multiple of 4 and at most n_max");
+  if (n == 0) return QZ_OK;
+  if (!in || !out || !peer_buffers || !aligned16(in) || !aligned16(out))
+    return fail(QZ_ERR_INVALID, "qz_allreduce_sum: null or unaligned pointer");
+  qz::comm::Peers peers{};
+  for (int j = 0; j < ranks; ++j) {
+    if (!peer_buffers[j] || !aligned16(peer_buffers[j]))
+      return fail(QZ_ERR_INVALID, "qz_allreduce_sum: null or unaligned peer buffer");
+    peers.base[j] = static_cast<float*>(peer_buffers[j]);
+  }
+  // one CTA per 1024 float4 (4096 floats), at most kMaxBlocks
+  const int64_t n4 = n / 4;
+  const int nb = static_cast<int>(std::max<int64_t>(
+      1, std::min<int64_t>(qz::comm::kMaxBlocks, qz::cdiv(n4, 256))));
+  qz::comm::allreduce_kernel<<<nb, qz::comm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      in, out, n, n_max, peers, rank, ranks);
+  QZ_CUDA(cudaGetLastError());
+  return QZ_OK;
 }
 
 int qz_attention_prefill(const float* q, const float* k_cache, const float* v_cache, float* out,

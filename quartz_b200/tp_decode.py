@@ -102,10 +102,13 @@ class TPDecodeEngine(DecodeEngine):
 
     def __init__(self, spec: ModelSpec, int8_weights: Mapping | Iterable | None, norms: Mapping,
                  *, group=None, max_ctx: int, max_prefill: int = 512, device=None,
-                 presharded=None):
+                 presharded=None, allreduce: str = "peer"):
         """int8_weights: the full checkpoint (every rank slices its part with
         tp_shard), or None with presharded = tp_shard(...)'s result for this
-        rank (arrays may be torch tensors already on the device)."""
+        rank (arrays may be torch tensors already on the device).
+        allreduce: "peer" sums the per-token [H] partials with the
+        peer-memory kernel (quartz_b200.comm), "nccl" with the process
+        group's all-reduce; prefill's [M, H] sums always use NCCL."""
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -121,6 +124,20 @@ class TPDecodeEngine(DecodeEngine):
         self.ltok = torch.zeros(1, dtype=torch.int64, device=self.dev)
         self.pair = torch.zeros((1, 2), dtype=torch.float64, device=self.dev)
         self.pairs = torch.zeros((self.world, 2), dtype=torch.float64, device=self.dev)
+        if allreduce not in ("peer", "nccl"):
+            raise ValueError("allreduce must be 'peer' or 'nccl'")
+        self.peer = None
+        if allreduce == "peer" and self.world > 1:
+            from .comm import PeerAllReduce
+            self.peer = PeerAllReduce(self.spec.hidden, group=group, device=self.dev)
+
+    def close(self) -> None:
+        """Release the graph (it may hold collectives) and the peer buffers;
+        every rank calls it before the process group goes."""
+        self._graph = None
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def load_kv(self, kv: Iterable) -> None:
         """Per layer full (K, V) [n_kv, T, head_dim]: this rank keeps its kv heads."""
@@ -130,7 +147,10 @@ class TPDecodeEngine(DecodeEngine):
 
     # -------------------------------------------------------------- collectives
     def _all_reduce(self, t: torch.Tensor) -> None:
-        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
+        if self.peer is not None and t.numel() <= self.peer.n_max and t.numel() % 4 == 0:
+            self.peer(t)
+        else:
+            dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)
 
     def _pick_token(self, st: int, pos_step: int) -> None:
         """Greedy token over the vocab shards: local argmax, then one all-gather

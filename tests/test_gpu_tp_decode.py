@@ -45,11 +45,13 @@ def _worker(rank, world, port, cids):
             case = cases[cid]
             spec = ModelSpec.from_hf(case["cfg"], case["arch"])
             start = case.get("kv_len") or len(case["prompt"])
-            eng = TPDecodeEngine(spec, random_int8_weights(spec), norm_weights(spec),
-                                 max_ctx=start + case["steps"],
-                                 max_prefill=max(2, len(case.get("prompt", [])) or 2),
-                                 device=torch.device("cuda", rank))
-            for graph in (False, True):
+            for allreduce, graph in (("nccl", False), ("nccl", True), ("peer", False),
+                                     ("peer", True)):
+                if graph is False:
+                    eng = TPDecodeEngine(spec, random_int8_weights(spec), norm_weights(spec),
+                                         max_ctx=start + case["steps"],
+                                         max_prefill=max(2, len(case.get("prompt", [])) or 2),
+                                         device=torch.device("cuda", rank), allreduce=allreduce)
                 if case["start"] == "kv":
                     eng.load_kv(seeded_kv(spec, case["kv_len"]))
                     toks = eng.generate(case["first"], case["steps"], graph=graph, unroll=8)
@@ -57,10 +59,11 @@ def _worker(rank, world, port, cids):
                     eng.reset(0)
                     t0 = eng.prefill(case["prompt"])
                     toks = [t0] + eng.generate(t0, case["steps"] - 1, graph=graph, unroll=8)
-                assert toks == golds[cid], (cid, graph, rank)
-            eng._graph = None   # a graph holding NCCL calls goes before the process group
-            del eng
-            torch.cuda.synchronize()
+                assert toks == golds[cid], (cid, allreduce, graph, rank)
+                if graph:
+                    eng.close()   # the graph (it holds collectives) and the peer buffers
+                    del eng
+                    torch.cuda.synchronize()
         device.check_status(torch.device("cuda", rank))
     finally:
         torch.distributed.destroy_process_group()
@@ -69,7 +72,62 @@ def _worker(rank, world, port, cids):
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs 2 GPUs")
 def test_tp_decode_tokens_match_reference():
+    """NCCL and peer-memory all-reduces, eager and graph replay."""
     import torch.multiprocessing as mp
     mp.spawn(_worker, args=(2, _free_port(),
                             ["qwen3_small_kv", "llama_small_prompt", "qwen3_0p6b_kv512"]),
              nprocs=2, join=True)
+
+
+def _ar_worker(rank, world, port):
+    import sys
+    sys.path.insert(0, REPO)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    torch.distributed.init_process_group(
+        "nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+        timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    from quartz_b200 import device
+    from quartz_b200.comm import PeerAllReduce
+    try:
+        ar = PeerAllReduce(8192, device=torch.device("cuda", rank))
+        g = torch.Generator().manual_seed(5)
+        for n in (4, 1024, 4096, 8192, 4 * 777):
+            xs = [torch.randn(n, generator=g) for _ in range(world)]
+            ref = xs[0].clone()
+            for x in xs[1:]:
+                ref += x            # rank order, like the kernel
+            for rep in range(3):    # both parities, repeated calls
+                t = xs[rank].cuda()
+                out = ar(t)
+                assert torch.equal(out.cpu(), ref), (n, rep)
+        # many back-to-back calls in one CUDA graph
+        t = torch.full((4096,), float(rank + 1), device="cuda")
+        graph = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(graph, stream=s):
+                for _ in range(20):
+                    ar(t)
+                    t.mul_(1.0 / world)
+        torch.cuda.current_stream().wait_stream(s)
+        graph.replay()
+        torch.cuda.synchronize()
+        total = world * (world + 1) / 2 / world
+        assert torch.allclose(t, torch.full_like(t, total)), float(t[0])
+        del graph
+        ar.close()
+        device.check_status(torch.device("cuda", rank))
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
+                    reason="needs 2 GPUs")
+def test_peer_allreduce_exact():
+    """The peer-memory sum equals the rank-order fp32 sum bit for bit, on both
+    buffer parities and inside a CUDA graph."""
+    import torch.multiprocessing as mp
+    world = min(torch.cuda.device_count(), 4)
+    mp.spawn(_ar_worker, args=(world, _free_port()), nprocs=world, join=True)
