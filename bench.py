@@ -467,36 +467,42 @@ def run_tp_decode(args, rank: int, world: int, dev) -> dict:
     from quartz_b200.model import QWEN3_8B, norm_weights
     from quartz_b200.tp_decode import TPDecodeEngine, random_tp_shard
     spec = QWEN3_8B
-    shard = random_tp_shard(spec, rank, world, dev)
-    eng = TPDecodeEngine(spec, None, norm_weights(spec), max_ctx=TP_CTX + TP_TOKENS,
-                         max_prefill=1, device=dev, presharded=shard)
-    del shard
     stream = torch.cuda.current_stream()
 
-    def one_pass():
-        eng.reset(TP_CTX)
-        eng.tok.fill_(7)
-        for _ in range(TP_TOKENS // TP_UNROLL):
-            eng.replay()
+    def measure(allreduce: str) -> float:
+        shard = random_tp_shard(spec, rank, world, dev)
+        eng = TPDecodeEngine(spec, None, norm_weights(spec), max_ctx=TP_CTX + TP_TOKENS,
+                             max_prefill=1, device=dev, presharded=shard, allreduce=allreduce)
+        del shard
 
-    eng.reset(TP_CTX)
-    eng.capture(TP_UNROLL)
-    for _ in range(2):
-        one_pass()
-    torch.cuda.synchronize()
-    passes = 3
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    _barrier(world)
-    e0.record(stream)
-    for _ in range(passes):
-        one_pass()
-    e1.record(stream)
-    _barrier(world)
-    ms_tok = _dist_max(e0.elapsed_time(e1) / (passes * TP_TOKENS), world)
-    eng._graph = None        # a graph holding NCCL calls goes before the process group
-    del eng
-    torch.cuda.empty_cache()
+        def one_pass():
+            eng.reset(TP_CTX)
+            eng.tok.fill_(7)
+            for _ in range(TP_TOKENS // TP_UNROLL):
+                eng.replay()
+
+        eng.reset(TP_CTX)
+        eng.capture(TP_UNROLL)
+        for _ in range(2):
+            one_pass()
+        torch.cuda.synchronize()
+        passes = 3
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        _barrier(world)
+        e0.record(stream)
+        for _ in range(passes):
+            one_pass()
+        e1.record(stream)
+        _barrier(world)
+        ms = _dist_max(e0.elapsed_time(e1) / (passes * TP_TOKENS), world)
+        eng.close()          # the graph (it holds collectives) and the peer buffers
+        del eng
+        torch.cuda.empty_cache()
+        return ms
+
+    ms_tok = measure("peer")
+    ms_nccl = measure("nccl") if world > 1 else ms_tok
     wbytes = spec.int8_bytes_per_token()
     kvbytes = spec.kv_bytes_per_token(TP_CTX + TP_TOKENS // 2)
     peak, peak_kind = _peaks()
@@ -510,7 +516,10 @@ def run_tp_decode(args, rank: int, world: int, dev) -> dict:
             "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                          "unit": UNIT, "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "per": "one GPU (its 1/N of the bytes)"},
-            "collectives_per_token": 2 * spec.layers + 1}
+            "collectives_per_token": 2 * spec.layers + 1,
+            "allreduce": "peer-memory kernel (qz_allreduce_sum)" if world > 1 else "none",
+            "with_nccl_allreduce": {"us_per_token": round(ms_nccl * 1e3, 1),
+                                    "value": round(1.0 / (ms_nccl * 1e-3), 1)}}
 
 
 def run_ours(args, rank: int, world: int, local: int) -> dict | None:

@@ -58,16 +58,45 @@ __global__ void embed_gather_kernel(const int8_t* __restrict__ q, const float* _
     out[m * H + h] = static_cast<float>(q[id * H + h]) * scale[id * ng + h / G];
 }
 
-// One block per row: y = x * (1 / sqrt(mean(x^2) + eps)) * w.
-__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w,
-                               float* __restrict__ y, int64_t n, float eps) {
+// One block per row: y = x * (1 / sqrt(mean(x^2) + eps)) * w. The first
+// kNormPer x kNormThreads elements (4096) are loaded in one unrolled round
+// (x and w together) and kept in registers, so a row costs one memory round
+// trip instead of one per loop iteration.
+constexpr int kNormThreads = 512;
+constexpr int kNormPer = 8;
+__global__ void __launch_bounds__(kNormThreads) rmsnorm_kernel(const float* __restrict__ x,
+                                                               const float* __restrict__ w,
+                                                               float* __restrict__ y, int64_t n,
+                                                               float eps) {
   __shared__ float red[32];
   const float* xr = x + blockIdx.x * n;
+  float* yr = y + blockIdx.x * n;
+  constexpr int64_t kBatch = static_cast<int64_t>(kNormPer) * kNormThreads;
+  float v[kNormPer], wv[kNormPer];
   float ss = 0.f;
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+#pragma unroll
+  for (int k = 0; k < kNormPer; ++k) {
+    const int64_t i = threadIdx.x + static_cast<int64_t>(k) * kNormThreads;
+    v[k] = i < n ? xr[i] : 0.f;
+    wv[k] = i < n ? w[i] : 0.f;
+    ss = fmaf(v[k], v[k], ss);
+  }
+  for (int64_t base = kBatch; base < n; base += kBatch) {
+#pragma unroll
+    for (int k = 0; k < kNormPer; ++k) {
+      const int64_t i = base + threadIdx.x + static_cast<int64_t>(k) * kNormThreads;
+      const float t = i < n ? xr[i] : 0.f;
+      ss = fmaf(t, t, ss);
+    }
+  }
   ss = block_sum(ss, red);
   const float r = 1.0f / sqrtf(ss / static_cast<float>(n) + eps);
-  for (int64_t i = threadIdx.x; i < n; i += blockDim.x) y[blockIdx.x * n + i] = xr[i] * r * w[i];
+#pragma unroll
+  for (int k = 0; k < kNormPer; ++k) {
+    const int64_t i = threadIdx.x + static_cast<int64_t>(k) * kNormThreads;
+    if (i < n) yr[i] = v[k] * r * wv[k];
+  }
+  for (int64_t i = kBatch + threadIdx.x; i < n; i += kNormThreads) yr[i] = xr[i] * r * w[i];
 }
 
 // qkv: [M, (nq + 2 nkv) * hd] (q heads, k heads, v heads). One block per

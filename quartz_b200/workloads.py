@@ -103,6 +103,8 @@ def mlp_algorithmic_bytes(H, I, ng=1, ngd=1, M=1) -> int:
 #   python -m quartz_b200.workloads decode [--persistent] [--tokens T]
 #                                                   Qwen3-0.6B, 512 prefilled KV
 #                                                   positions, T eager tokens
+#   python -m quartz_b200.workloads decode8b [--tokens T]
+#                                                   Qwen3-8B shapes, context 2048
 #   python -m quartz_b200.workloads prefill         Llama-3.2-1B 512-token prefill
 # ---------------------------------------------------------------------------
 def _main(argv=None) -> None:
@@ -120,6 +122,8 @@ def _main(argv=None) -> None:
     d = sub.add_parser("decode")
     d.add_argument("--persistent", action="store_true")
     d.add_argument("--tokens", type=int, default=3)
+    d8 = sub.add_parser("decode8b")
+    d8.add_argument("--tokens", type=int, default=3)
     sub.add_parser("prefill")
     a = ap.parse_args(argv)
     dev = torch.device("cuda", 0)
@@ -150,6 +154,17 @@ def _main(argv=None) -> None:
             eng.load_kv(seeded_kv(spec, 512))
             toks = eng.generate(42, a.tokens, graph=False)
             print(f"decode ({'persistent' if eng.persistent else 'per-op'}): {toks}")
+        elif a.what == "decode8b":
+            # Qwen3-8B shapes on one GPU, device-drawn weights, context 2048
+            from .model import QWEN3_8B
+            from .tp_decode import random_tp_shard
+            local, w, (lq, ls, _, _) = random_tp_shard(QWEN3_8B, 0, 1, dev)
+            eng = DecodeEngine(local, w, norm_weights(QWEN3_8B), max_ctx=2048 + a.tokens,
+                               max_prefill=1, device=dev)
+            eng.lm_q, eng.lm_s = lq, ls
+            eng.reset(2048)
+            toks = eng.generate(7, a.tokens, graph=False)
+            print(f"decode8b: {toks}")
         else:
             spec = LLAMA_3P2_1B
             eng = DecodeEngine(spec, random_int8_weights(spec), norm_weights(spec), max_ctx=600,
