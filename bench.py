@@ -332,6 +332,33 @@ def run_decode(args, dev, world: int = 1) -> dict:
 
     ms_tok, e2e_ms, launches = measure(False)
     ms_p, _, launches_p = measure(True)
+    cpu = None
+    if world == 1 and not args.no_cpu:
+        # the oracle's CPU decode port (numpy glue + the C/OpenMP restatement of
+        # quartz's int8 kernels) on a bounded sample: 8 tokens after the 512
+        # prefilled positions, all host cores
+        import oracle
+        from oracle.decode_port import DecodePort
+        cfg = dict(hidden_size=spec.hidden, num_hidden_layers=spec.layers,
+                   num_attention_heads=spec.n_heads, num_key_value_heads=spec.n_kv,
+                   head_dim=spec.head_dim, intermediate_size=spec.inter, vocab_size=spec.vocab,
+                   rope_theta=spec.rope_theta, tie_word_embeddings=spec.tie, rms_norm_eps=spec.eps)
+        oracle.set_threads(_cpu_cores())
+        port = DecodePort(cfg, spec.arch, dict((n, (q, s_)) for n, q, s_ in weights),
+                          norm_weights(spec), max_ctx=DECODE_KV + 8)
+        port.load_kv(kv)
+        tok = port.step(DECODE_FIRST)          # warm-up (first-touch of the weights)
+        t0 = time.perf_counter()
+        toks = []
+        for _ in range(7):
+            tok = port.step(tok)
+            toks.append(tok)
+        dt = (time.perf_counter() - t0) / 7
+        if toks != gold[1:8]:
+            raise SystemExit("CPU decode port disagrees with the reference tokens")
+        cpu = {"value": round(1.0 / dt, 2), "unit": "tok/s", "cores": oracle.threads(),
+               "kind": "port", "sample": "7 greedy tokens after the 512 prefilled positions "
+                                        f"({dt * 1e3:.1f} ms per token)"}
     wbytes = spec.int8_bytes_per_token()
     ctx_mean = DECODE_KV + (DECODE_TOKENS + 1) / 2
     kvbytes = spec.kv_bytes_per_token(int(round(ctx_mean)))
@@ -350,6 +377,7 @@ def run_decode(args, dev, world: int = 1) -> dict:
                     "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 8 * DECODE_TOKENS,
                     "note": "DecodeEngine.generate per 128-token pass (first token in, "
                             "token list out)"},
+            "cpu_baseline": cpu,
             "persistent_kernel": {"value": round(world / (ms_p * 1e-3), 1), "unit": "tok/s",
                                   "us_per_token": round(ms_p * 1e3, 2),
                                   "launches_per_token": launches_p},

@@ -296,7 +296,8 @@ int qz_ipc_close(void* ptr);
  * mapped in this process (this rank's own at [rank]). Every rank must make
  * the same sequence of calls on its buffer; a call waits for its peers' pushes
  * for at most about a second (then the status word records it). in may equal
- * out. n a multiple of 4, in/out 16-byte aligned.
+ * out. Each value travels with the call's tag in one 8-byte word, so a
+ * receiver polls the data itself (no separate flag, no fence).
  */
 int qz_allreduce_sum(const float* in, float* out, int64_t n, int64_t n_max,
                      void* const* peer_buffers, int rank, int ranks, void* stream);

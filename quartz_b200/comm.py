@@ -3,9 +3,10 @@
 Every rank allocates one communication buffer with the library (its own
 cudaMalloc, so its CUDA IPC handle covers exactly that range), the ranks swap
 handles once through the process group, and each rank maps its peers'
-buffers. A sum is then one kernel per rank that pushes its slice to every
-peer over NVLink, waits (bounded) for the peers' flags and adds the slots in
-rank order, so every rank gets bit-identical results. Small messages only:
+buffers. A sum is then one kernel per rank that pushes its values, each
+tagged with the call's epoch in one 8-byte word, to every peer over NVLink,
+polls (bounded) until the peers' words of this call have arrived and adds
+them in rank order, so every rank gets bit-identical results. Small messages only:
 the [H] partials of a tensor-parallel decode step, where a library
 all-reduce's fixed latency dominates.
 """
@@ -62,8 +63,8 @@ class PeerAllReduce:
         n = t.numel()
         if t.dtype != torch.float32 or not t.is_contiguous() or out.numel() != n:
             raise ValueError("fp32 contiguous tensors of equal size expected")
-        if n > self.n_max or n % 4:
-            raise ValueError(f"{n} elements: at most {self.n_max}, a multiple of 4")
+        if n > self.n_max:
+            raise ValueError(f"{n} elements: at most {self.n_max}")
         _lib.check(self.lib.qz_allreduce_sum(t.data_ptr(), out.data_ptr(), n, self.n_max,
                                              self._peers, self.rank, self.world,
                                              torch.cuda.current_stream(self.dev).cuda_stream))

@@ -1056,21 +1056,20 @@ int qz_allreduce_sum(const float* in, float* out, int64_t n, int64_t n_max,
                      void* const* peer_buffers, int rank, int ranks, void* stream) {
   if (ranks < 1 || ranks > qz::comm::kMaxRanks || rank < 0 || rank >= ranks)
     return fail(QZ_ERR_INVALID, "qz_allreduce_sum: bad rank / rank count");
-  if (n < 0 || n > n_max || n % 4 || n_max % 4)
-    return fail(QZ_ERR_INVALID, "qz_allreduce_sum: n must be a multiple of 4 and at most n_max");
+  if (n < 0 || n > n_max || n_max % 4)
+    return fail(QZ_ERR_INVALID, "qz_allreduce_sum: n must be at most n_max (a multiple of 4)");
   if (n == 0) return QZ_OK;
-  if (!in || !out || !peer_buffers || !aligned16(in) || !aligned16(out))
-    return fail(QZ_ERR_INVALID, "qz_allreduce_sum: null or unaligned pointer");
+  if (!in || !out || !peer_buffers)
+    return fail(QZ_ERR_INVALID, "qz_allreduce_sum: null pointer");
   qz::comm::Peers peers{};
   for (int j = 0; j < ranks; ++j) {
     if (!peer_buffers[j] || !aligned16(peer_buffers[j]))
       return fail(QZ_ERR_INVALID, "qz_allreduce_sum: null or unaligned peer buffer");
     peers.base[j] = static_cast<float*>(peer_buffers[j]);
   }
-  // one CTA per 1024 float4 (4096 floats), at most kMaxBlocks
-  const int64_t n4 = n / 4;
+  // one CTA per 1024 elements, at most kMaxBlocks
   const int nb = static_cast<int>(std::max<int64_t>(
-      1, std::min<int64_t>(qz::comm::kMaxBlocks, qz::cdiv(n4, 256))));
+      1, std::min<int64_t>(qz::comm::kMaxBlocks, qz::cdiv(n, 1024))));
   qz::comm::allreduce_kernel<<<nb, qz::comm::kThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       in, out, n, n_max, peers, rank, ranks);
   QZ_CUDA(cudaGetLastError());

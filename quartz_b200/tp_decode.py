@@ -147,7 +147,7 @@ class TPDecodeEngine(DecodeEngine):
 
     # -------------------------------------------------------------- collectives
     def _all_reduce(self, t: torch.Tensor) -> None:
-        if self.peer is not None and t.numel() <= self.peer.n_max and t.numel() % 4 == 0:
+        if self.peer is not None and t.numel() <= self.peer.n_max:
             self.peer(t)
         else:
             dist.all_reduce(t, op=dist.ReduceOp.SUM, group=self.group)

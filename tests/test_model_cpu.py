@@ -185,3 +185,21 @@ def test_tp_shard_reassembles(cid, world):
     assert [p[2][2] for p in parts] == [0] + [p[2][3] for p in parts][:-1]
     with pytest.raises(ValueError):
         tp_shard(spec, w, 0, 3)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_tp_shard_eight_kv_heads(world):
+    """Qwen3-8B's head counts (32 query / 8 kv, MLP a multiple of 8) split over
+    1, 2, 4 and 8 ranks, on a small stand-in of the same head structure."""
+    from quartz_b200.tp_decode import tp_shard
+    spec = ModelSpec(arch="Qwen3ForCausalLM", hidden=64, layers=1, n_heads=32, n_kv=8,
+                     head_dim=16, inter=96, vocab=50, rope_theta=1e6, tie=False)
+    w = {n: (q, s) for n, q, s in random_int8_weights(spec)}
+    parts = [tp_shard(spec, w, r, world) for r in range(world)]
+    for local, lw, (lq, _, lo, hi) in parts:
+        assert local.n_heads == 32 // world and local.n_kv == 8 // world
+        assert lw["model.layers.0.self_attn.q_proj"][0].shape == (32 // world * 16, 64)
+        assert lw["model.layers.0.self_attn.o_proj"][0].shape == (64, 32 // world * 16)
+        assert lw["model.layers.0.mlp.down_proj"][0].shape == (64, 96 // world)
+        assert lq.shape[0] == hi - lo
+    assert sum(p[2][3] - p[2][2] for p in parts) == 50
