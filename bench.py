@@ -529,7 +529,8 @@ def run_tp_decode(args, rank: int, world: int, dev) -> dict:
         torch.cuda.empty_cache()
         return ms
 
-    ms_tok = measure("peer")
+    ms_tok = measure("fused")
+    ms_peer = measure("peer") if world > 1 else ms_tok
     ms_nccl = measure("nccl") if world > 1 else ms_tok
     wbytes = spec.int8_bytes_per_token()
     kvbytes = spec.kv_bytes_per_token(TP_CTX + TP_TOKENS // 2)
@@ -545,7 +546,10 @@ def run_tp_decode(args, rank: int, world: int, dev) -> dict:
                          "unit": UNIT, "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                          "per": "one GPU (its 1/N of the bytes)"},
             "collectives_per_token": 2 * spec.layers + 1,
-            "allreduce": "peer-memory kernel (qz_allreduce_sum)" if world > 1 else "none",
+            "allreduce": ("in the kernels: GEMV / MLP epilogues push to peer memory, the next "
+                          "RMSNorm sums") if world > 1 else "none",
+            "with_peer_allreduce_kernel": {"us_per_token": round(ms_peer * 1e3, 1),
+                                           "value": round(1.0 / (ms_peer * 1e-3), 1)},
             "with_nccl_allreduce": {"us_per_token": round(ms_nccl * 1e3, 1),
                                     "value": round(1.0 / (ms_nccl * 1e-3), 1)}}
 

@@ -302,6 +302,37 @@ int qz_ipc_close(void* ptr);
 int qz_allreduce_sum(const float* in, float* out, int64_t n, int64_t n_max,
                      void* const* peer_buffers, int rank, int ranks, void* stream);
 
+/* Fused all-reduce: a producer kernel (qz_gemv_w8_peer,
+ * qz_fused_mlp_decode_peer) sends its output rows, tagged with the call, to
+ * every rank's buffer (region B of qz_comm_buffer_bytes) from its epilogue,
+ * instead of writing them; qz_rmsnorm_peer_sum on each rank then sums the
+ * ranks' rows in rank order as it reads them and applies an RMSNorm. The
+ * partial sums of a row-parallel projection are reduced without a separate
+ * collective launch. Producers and consumers must alternate, in the same order
+ * on every rank. */
+typedef struct {
+  void* buffers[8];   /* every rank's qz_comm_alloc buffer as mapped in this process */
+  int rank;
+  int ranks;          /* 1..8 */
+  int64_t n_max;      /* the buffers' n_max (qz_comm_buffer_bytes) */
+} qz_peer_sum;
+
+/* qz_gemv_w8 whose rows y[n] (+ residual[n]) go to the ranks (no local y). */
+int qz_gemv_w8_peer(const int8_t* q, const float* scale, int64_t ng, const float* x, int64_t N,
+                    int64_t K, const float* residual, const qz_peer_sum* ps, void* stream);
+
+/* qz_fused_mlp_decode whose output rows (+ residual) go to the ranks. */
+int qz_fused_mlp_decode_peer(const int8_t* gu_q, const float* gu_s, int64_t ng, const float* x,
+                             const int8_t* down_q, const float* down_s, int64_t ngd, float* abuf,
+                             const float* residual, int64_t H, int64_t I, uint32_t* sync_ws,
+                             const qz_peer_sum* ps, void* stream);
+
+/* h[i] = sum over ranks (rank order) of the rows the last producer pushed,
+ * i < n (n <= 4096); xn = h / sqrt(mean(h^2) + eps) * w (quartz/ops.py:24-32).
+ * Waits for the pushes for at most about a second (status word). */
+int qz_rmsnorm_peer_sum(const qz_peer_sum* ps, int64_t n, const float* w, float eps, float* h,
+                        float* xn, void* stream);
+
 /* Read the device status word of the current device into words[0..3]
  * ({error bits, first error site, block of first error, error count}); when
  * clear != 0 reset it to zero afterwards. Synchronises the device. */

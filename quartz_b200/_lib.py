@@ -59,6 +59,10 @@ SIGNATURES = {
     "qz_ipc_open": ([_vp, ctypes.POINTER(_vp)], _int),
     "qz_ipc_close": ([_vp], _int),
     "qz_allreduce_sum": ([_vp, _vp, _i64, _i64, _vp, _int, _int, _vp], _int),
+    "qz_gemv_w8_peer": ([_vp, _vp, _i64, _vp, _i64, _i64, _vp, _vp, _vp], _int),
+    "qz_fused_mlp_decode_peer": ([_vp, _vp, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64,
+                                  _vp, _vp, _vp], _int),
+    "qz_rmsnorm_peer_sum": ([_vp, _i64, _vp, ctypes.c_float, _vp, _vp, _vp], _int),
     "qz_decode_layers": ([_vp, _int, _vp, _vp, _i64, _vp, _vp, _vp, _vp, _vp, _int, _int, _int,
                           _int, _int, _i64, ctypes.c_float, ctypes.c_float, _vp, ctypes.c_size_t,
                           _vp, _vp], _int),

@@ -21,6 +21,13 @@ import torch.distributed as dist
 from . import _lib
 
 
+class PeerSum(ctypes.Structure):
+    """qz_peer_sum: every rank's buffer as mapped here, this rank, the rank
+    count, the buffers' n_max."""
+    _fields_ = [("buffers", ctypes.c_void_p * 8), ("rank", ctypes.c_int),
+                ("ranks", ctypes.c_int), ("n_max", ctypes.c_int64)]
+
+
 class PeerAllReduce:
     """In-place sums of fp32 CUDA tensors of at most `n_max` elements over the
     ranks of `group` (one GPU per rank, peer access between them). Every rank
@@ -55,6 +62,7 @@ class PeerAllReduce:
                 self._opened.append(p.value)
                 ptrs.append(p.value)
         self._peers = (ctypes.c_void_p * self.world)(*ptrs)
+        self.ps = PeerSum((ctypes.c_void_p * 8)(*ptrs), self.rank, self.world, self.n_max)
         dist.barrier(group=group)
 
     def __call__(self, t: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:

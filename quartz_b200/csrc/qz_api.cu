@@ -214,14 +214,18 @@ int launch_gemv_k(const DeviceInfo& d, const qz::GemvArgs& a, cudaStream_t st) {
 }
 
 int gemv_impl(const int8_t* q, const float* scale, int64_t ng, const float* x, float* y,
-              int64_t N, int64_t K, const float* residual, cudaStream_t st) {
+              int64_t N, int64_t K, const float* residual, cudaStream_t st,
+              const qz::comm::PeerOut* po = nullptr) {
   DeviceInfo* d = nullptr;
   if (int rc = device_info(&d)) return rc;
   const int64_t G = K / ng;
   const bool fits = qz::stream_smem_bytes(kTallRows, K) <= d->smem_optin - 256;
   const bool fast = K > 0 && K % 16 == 0 && G % 16 == 0 && aligned16(q) && fits;
+  if (!fast && po)
+    return fail(QZ_ERR_UNSUPPORTED, "qz_gemv_w8_peer: shape outside the streaming kernel");
   if (!fast) return launch_generic_gemm(*d, q, scale, ng, x, y, residual, 1, N, K, st);
-  const qz::GemvArgs a{q, scale, x, y, residual, N, K, ng};
+  qz::GemvArgs a{q, scale, x, y, residual, N, K, ng};
+  if (po) a.po = *po;
   // Tall grouping unless it would leave SMs without a CTA.
   const bool tall = qz::cdiv(N, int64_t(kTallRows) * qz::kWarps) >= d->sms;
   if (ng == 1)
@@ -462,14 +466,17 @@ int qz_gemm_w8_ws(const int8_t* q, const float* scale, int64_t ng, const float* 
 
 int qz_mlp_workspace_bytes(void) { return 256; }
 
-int qz_fused_mlp_decode(const int8_t* gu_q, const float* gu_s, int64_t ng, const float* x,
-                        const int8_t* down_q, const float* down_s, int64_t ngd, float* abuf,
-                        float* out, const float* residual, int64_t H, int64_t I,
-                        uint32_t* sync_ws, void* stream) {
+}  // extern "C"
+
+namespace {
+int mlp_impl(const int8_t* gu_q, const float* gu_s, int64_t ng, const float* x,
+             const int8_t* down_q, const float* down_s, int64_t ngd, float* abuf, float* out,
+             const float* residual, int64_t H, int64_t I, uint32_t* sync_ws, void* stream,
+             const qz::comm::PeerOut* po) {
   if (int rc = check_weights(gu_q, gu_s, ng, 2 * I, H, "qz_fused_mlp_decode (gate|up)")) return rc;
   if (int rc = check_weights(down_q, down_s, ngd, H, I, "qz_fused_mlp_decode (down)")) return rc;
   if (H == 0) return QZ_OK;
-  if (!out || (I > 0 && !abuf) || !x)
+  if ((!out && !po) || (I > 0 && !abuf) || !x)
     return fail(QZ_ERR_INVALID, "qz_fused_mlp_decode: null x, abuf or out");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   DeviceInfo* d = nullptr;
@@ -479,6 +486,8 @@ int qz_fused_mlp_decode(const int8_t* gu_q, const float* gu_s, int64_t ng, const
   const bool fast = I > 0 && H % 16 == 0 && I % 16 == 0 && (H / ng) % 16 == 0 &&
                     (I / ngd) % 16 == 0 && aligned16(gu_q) && aligned16(down_q) && fits &&
                     sync_ws != nullptr && d->coop;
+  if (!fast && po)
+    return fail(QZ_ERR_UNSUPPORTED, "qz_fused_mlp_decode_peer: shape outside the fused kernel");
   if (!fast) {
     // Two launches: gate/up + SiLU into abuf, then the down GEMV.
     if (I > 0) {
@@ -489,13 +498,76 @@ int qz_fused_mlp_decode(const int8_t* gu_q, const float* gu_s, int64_t ng, const
     }
     return launch_generic_gemm(*d, down_q, down_s, ngd, abuf, out, residual, 1, H, I, st);
   }
-  const qz::MlpArgs a{gu_q, gu_s, x, down_q, down_s, abuf, out, residual, sync_ws, H, I, ng, ngd};
+  qz::MlpArgs a{gu_q, gu_s, x, down_q, down_s, abuf, out, residual, sync_ws, H, I, ng, ngd};
+  if (po) a.po = *po;
   const bool per_row = ng == 1 && ngd == 1;
   // Tall groups (2 units = 4 rows) unless too few units to fill the SMs.
   const bool tall = qz::cdiv(I, int64_t(kTallRows / 2) * qz::kWarps) >= d->sms;
   if (per_row)
     return tall ? launch_mlp_k<kTallRows, true>(*d, a, st) : launch_mlp_k<2, true>(*d, a, st);
   return tall ? launch_mlp_k<kTallRows, false>(*d, a, st) : launch_mlp_k<2, false>(*d, a, st);
+}
+
+int peer_out(const qz_peer_sum* ps, int64_t n, qz::comm::PeerOut* po, const char* what) {
+  if (!ps || ps->ranks < 1 || ps->ranks > qz::comm::kMaxRanks || ps->rank < 0 ||
+      ps->rank >= ps->ranks || ps->n_max % 4 || n > ps->n_max)
+    return fail(QZ_ERR_INVALID, std::string(what) + ": bad qz_peer_sum (ranks, rank, n_max)");
+  *po = qz::comm::PeerOut{};
+  for (int j = 0; j < ps->ranks; ++j) {
+    if (!ps->buffers[j] || !aligned16(ps->buffers[j]))
+      return fail(QZ_ERR_INVALID, std::string(what) + ": null or unaligned peer buffer");
+    po->base[j] = static_cast<float*>(ps->buffers[j]);
+  }
+  po->rank = ps->rank;
+  po->P = ps->ranks;
+  po->n_max = ps->n_max;
+  return QZ_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int qz_fused_mlp_decode(const int8_t* gu_q, const float* gu_s, int64_t ng, const float* x,
+                        const int8_t* down_q, const float* down_s, int64_t ngd, float* abuf,
+                        float* out, const float* residual, int64_t H, int64_t I,
+                        uint32_t* sync_ws, void* stream) {
+  return mlp_impl(gu_q, gu_s, ng, x, down_q, down_s, ngd, abuf, out, residual, H, I, sync_ws,
+                  stream, nullptr);
+}
+
+int qz_fused_mlp_decode_peer(const int8_t* gu_q, const float* gu_s, int64_t ng, const float* x,
+                             const int8_t* down_q, const float* down_s, int64_t ngd, float* abuf,
+                             const float* residual, int64_t H, int64_t I, uint32_t* sync_ws,
+                             const qz_peer_sum* ps, void* stream) {
+  qz::comm::PeerOut po;
+  if (int rc = peer_out(ps, H, &po, "qz_fused_mlp_decode_peer")) return rc;
+  return mlp_impl(gu_q, gu_s, ng, x, down_q, down_s, ngd, abuf, nullptr, residual, H, I, sync_ws,
+                  stream, &po);
+}
+
+int qz_gemv_w8_peer(const int8_t* q, const float* scale, int64_t ng, const float* x, int64_t N,
+                    int64_t K, const float* residual, const qz_peer_sum* ps, void* stream) {
+  if (int rc = check_weights(q, scale, ng, N, K, "qz_gemv_w8_peer")) return rc;
+  if (N == 0) return QZ_OK;
+  if (K > 0 && !x) return fail(QZ_ERR_INVALID, "qz_gemv_w8_peer: null x");
+  qz::comm::PeerOut po;
+  if (int rc = peer_out(ps, N, &po, "qz_gemv_w8_peer")) return rc;
+  return gemv_impl(q, scale, ng, x, nullptr, N, K, residual, static_cast<cudaStream_t>(stream),
+                   &po);
+}
+
+int qz_rmsnorm_peer_sum(const qz_peer_sum* ps, int64_t n, const float* w, float eps, float* h,
+                        float* xn, void* stream) {
+  qz::comm::PeerOut po;
+  if (int rc = peer_out(ps, n, &po, "qz_rmsnorm_peer_sum")) return rc;
+  if (n < 1 || n > qz::comm::kSumThreads * qz::comm::kSumPer)
+    return fail(QZ_ERR_INVALID, "qz_rmsnorm_peer_sum: n must be in [1, 4096]");
+  if (!w || !h || !xn) return fail(QZ_ERR_INVALID, "qz_rmsnorm_peer_sum: null pointer");
+  qz::comm::rmsnorm_peer_sum_kernel<<<1, qz::comm::kSumThreads, 0,
+                                      static_cast<cudaStream_t>(stream)>>>(
+      po.base[po.rank], po.P, po.n_max, h, w, xn, n, eps);
+  QZ_CUDA(cudaGetLastError());
+  return QZ_OK;
 }
 
 }  // extern "C"

@@ -24,6 +24,7 @@
 #pragma once
 
 #include "qz_device.cuh"
+#include "qz_peer.cuh"
 
 namespace qz {
 
@@ -59,6 +60,7 @@ struct GemvArgs {
   float* y;               // [N]
   const float* residual;  // [N] or null
   int64_t N, K, ng;
+  comm::PeerOut po;       // po.P > 0: push the rows to the ranks instead of writing y
 };
 
 struct MlpArgs {
@@ -72,6 +74,7 @@ struct MlpArgs {
   const float* residual;  // [H] or null
   unsigned int* sync_ws;  // grid barrier words {count, generation}, zero at first use
   int64_t H, I, ng, ngd;
+  comm::PeerOut po;       // po.P > 0: push the rows to the ranks instead of writing out
 };
 
 // ---------------------------------------------------------------------------
@@ -367,13 +370,22 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_kernel(const GemvArgs a) 
     const int64_t row = r0 + g * R + r;
     return row < r1 ? __ldg(a.scale + row * a.ng + grp) : 0.f;
   };
+  // a fused all-reduce's producer pushes each row, tagged with the call of
+  // the channel's epoch (stream-ordered: read after griddepcontrol.wait)
+  unsigned ptag = 0u;
+  if (a.po.P > 0)
+    ptag = *reinterpret_cast<volatile unsigned*>(
+        comm::fused_epoch(comm::own_base(a.po), a.po.P, a.po.n_max)) + 1u;
   auto done = [&](int64_t g, float s) {
     const int r = reduced_row<R>(lane);
     const int64_t row = r0 + g * R + r;
     if (r >= 0 && row < r1) {
       float o = PER_ROW ? s * __ldg(a.scale + row) : s;
       if (a.residual) o += a.residual[row];
-      a.y[row] = o;
+      if (a.po.P > 0)
+        comm::peer_push(a.po, ptag, static_cast<int>((ptag - 1u) & 1u), row, o);
+      else
+        a.y[row] = o;
     }
   };
   auto beyond = [&]() { cp_async_commit(); };
@@ -491,12 +503,19 @@ __global__ void __launch_bounds__(kThreads, MINB) fused_mlp_kernel(const MlpArgs
   auto scale2 = [&](int64_t g, int, int64_t grp) -> float {
     return h0 + g < h1 ? __ldg(a.down_s + (h0 + g) * a.ngd + grp) : 0.f;
   };
+  unsigned ptag = 0u;
+  if (a.po.P > 0)
+    ptag = *reinterpret_cast<volatile unsigned*>(
+        comm::fused_epoch(comm::own_base(a.po), a.po.P, a.po.n_max)) + 1u;
   auto done2 = [&](int64_t g, float s) {
     const int64_t row = h0 + g;
     if (lane == 0 && row < h1) {
       float o = PER_ROW ? s * __ldg(a.down_s + row) : s;
       if (a.residual) o += a.residual[row];
-      a.out[row] = o;
+      if (a.po.P > 0)
+        comm::peer_push(a.po, ptag, static_cast<int>((ptag - 1u) & 1u), row, o);
+      else
+        a.out[row] = o;
     }
   };
   // phase 2 reads abuf from the staged copy (it was written by other CTAs)

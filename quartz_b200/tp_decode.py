@@ -23,6 +23,7 @@ rank ends each step with the same token and position.
 
 from __future__ import annotations
 
+import ctypes
 from typing import Iterable, Mapping
 
 import numpy as np
@@ -102,13 +103,16 @@ class TPDecodeEngine(DecodeEngine):
 
     def __init__(self, spec: ModelSpec, int8_weights: Mapping | Iterable | None, norms: Mapping,
                  *, group=None, max_ctx: int, max_prefill: int = 512, device=None,
-                 presharded=None, allreduce: str = "peer"):
+                 presharded=None, allreduce: str = "fused"):
         """int8_weights: the full checkpoint (every rank slices its part with
         tp_shard), or None with presharded = tp_shard(...)'s result for this
         rank (arrays may be torch tensors already on the device).
-        allreduce: "peer" sums the per-token [H] partials with the
-        peer-memory kernel (quartz_b200.comm), "nccl" with the process
-        group's all-reduce; prefill's [M, H] sums always use NCCL."""
+        allreduce: how the per-token [H] partials are summed. "fused": the
+        o-projection GEMV and the fused MLP push their rows to the ranks from
+        their epilogues and the following RMSNorm sums them as it reads
+        (no collective launches); "peer": the peer-memory all-reduce kernel
+        (quartz_b200.comm); "nccl": the process group's all-reduce. Prefill's
+        [M, H] sums always use NCCL."""
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -124,12 +128,15 @@ class TPDecodeEngine(DecodeEngine):
         self.ltok = torch.zeros(1, dtype=torch.int64, device=self.dev)
         self.pair = torch.zeros((1, 2), dtype=torch.float64, device=self.dev)
         self.pairs = torch.zeros((self.world, 2), dtype=torch.float64, device=self.dev)
-        if allreduce not in ("peer", "nccl"):
-            raise ValueError("allreduce must be 'peer' or 'nccl'")
+        if allreduce not in ("fused", "peer", "nccl"):
+            raise ValueError("allreduce must be 'fused', 'peer' or 'nccl'")
         self.peer = None
-        if allreduce == "peer" and self.world > 1:
+        self.fused_ar = allreduce == "fused" and self.world > 1
+        if allreduce in ("fused", "peer") and self.world > 1:
             from .comm import PeerAllReduce
             self.peer = PeerAllReduce(self.spec.hidden, group=group, device=self.dev)
+        if self.fused_ar:
+            self.peer_sum = ctypes.byref(self.peer.ps)
 
     def close(self) -> None:
         """Release the graph (it may hold collectives) and the peer buffers;
@@ -172,7 +179,47 @@ class TPDecodeEngine(DecodeEngine):
         self.pos_dev.add_(pos_step)
 
     # ------------------------------------------------------------- the token
+    def _decode_ops_fused(self, st: int) -> None:
+        """The token with the all-reduces inside the kernels: producers push,
+        the next RMSNorm sums (see the constructor's allreduce="fused")."""
+        S, lib, chk = self.spec, self.lib, _lib.check
+        H, hd, nq, nkv = S.hidden, S.head_dim, S.n_heads, S.n_kv
+        p = lambda t: t.data_ptr()  # noqa: E731
+        h_a, h_b, xn = p(self.h_a), p(self.h_b), p(self.xn)
+        first = self.rank == 0
+        ps = self.peer_sum
+        chk(lib.qz_embed_gather(p(self.embed_q), p(self.embed_s), self.embed_s.shape[1],
+                                p(self.tok), 1, S.vocab, H, h_a, st))
+        chk(lib.qz_rmsnorm(h_a, p(self.layers[0].in_w), xn, 1, H, S.eps, st))
+        for li, L in enumerate(self.layers):
+            kc, vc = p(self.k_cache[li]), p(self.v_cache[li])
+            chk(lib.qz_gemv_w8(p(L.qkv_q), p(L.qkv_s), L.qkv_s.shape[1], xn, p(self.qkv),
+                               S.qkv_rows, H, None, st))
+            chk(lib.qz_attention_decode_qkv(p(self.qkv), _ptr(L.qn_w), _ptr(L.kn_w),
+                                            p(self.inv_freq), kc, vc, p(self.ao), nq, nkv, hd,
+                                            self.max_ctx, 0, p(self.pos_dev), S.eps,
+                                            self.attn_scale, p(self.attn_ws),
+                                            self.attn_ws.numel(), st))
+            # o-projection partials (rank 0 adds the residual) go to every rank
+            chk(lib.qz_gemv_w8_peer(p(L.o_q), p(L.o_s), L.o_s.shape[1], p(self.ao), H, nq * hd,
+                                    h_a if first else None, ps, st))
+            chk(lib.qz_rmsnorm_peer_sum(ps, H, p(L.post_w), S.eps, h_b, xn, st))
+            chk(lib.qz_fused_mlp_decode_peer(p(L.gu_q), p(L.gu_s), L.gu_s.shape[1], xn,
+                                             p(L.down_q), p(L.down_s), L.down_s.shape[1],
+                                             p(self.abuf), h_b if first else None, H, S.inter,
+                                             p(self.mlp_ws), ps, st))
+            # the sum, normalised for what comes next (the next layer or the lm_head)
+            nw = self.layers[li + 1].in_w if li + 1 < len(self.layers) else self.norm_w
+            chk(lib.qz_rmsnorm_peer_sum(ps, H, p(nw), S.eps, h_a, xn, st))
+        n_local = self.vhi - self.vlo
+        if n_local > 0:
+            chk(lib.qz_gemv_w8(p(self.lm_q), p(self.lm_s), self.lm_s.shape[1], xn,
+                               p(self.logits), n_local, H, None, st))
+        self._pick_token(st, 1)
+
     def _decode_ops(self, st: int) -> None:
+        if self.fused_ar:
+            return self._decode_ops_fused(st)
         S, lib, chk = self.spec, self.lib, _lib.check
         H, hd, nq, nkv = S.hidden, S.head_dim, S.n_heads, S.n_kv
         p = lambda t: t.data_ptr()  # noqa: E731
@@ -207,8 +254,12 @@ class TPDecodeEngine(DecodeEngine):
         self._pick_token(st, 1)
 
     def _launches_per_token(self) -> int:
-        # embed + per layer (rmsnorm, qkv, attention, o, rmsnorm, mlp) + norm, lm, argmax x2
-        return 1 + 6 * self.spec.layers + 4
+        if self.fused_ar:
+            # embed, rmsnorm + per layer (qkv, attention, o, peer sum, mlp, peer sum) + lm, argmax
+            return 2 + 6 * self.spec.layers + 2
+        # embed + per layer (rmsnorm, qkv, attention, o, all-reduce, rmsnorm, mlp, all-reduce)
+        # + norm, lm, argmax x2
+        return 1 + (8 if self.peer is not None else 6) * self.spec.layers + 4
 
     def prefill(self, ids) -> int:
         """The prompt through the tensor-core GEMMs on each rank's shard, two

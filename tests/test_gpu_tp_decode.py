@@ -46,7 +46,7 @@ def _worker(rank, world, port, cids):
             spec = ModelSpec.from_hf(case["cfg"], case["arch"])
             start = case.get("kv_len") or len(case["prompt"])
             for allreduce, graph in (("nccl", False), ("nccl", True), ("peer", False),
-                                     ("peer", True)):
+                                     ("peer", True), ("fused", False), ("fused", True)):
                 if graph is False:
                     eng = TPDecodeEngine(spec, random_int8_weights(spec), norm_weights(spec),
                                          max_ctx=start + case["steps"],
@@ -72,7 +72,7 @@ def _worker(rank, world, port, cids):
 @pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
                     reason="needs 2 GPUs")
 def test_tp_decode_tokens_match_reference():
-    """NCCL and peer-memory all-reduces, eager and graph replay."""
+    """NCCL, peer-memory and in-kernel (fused) all-reduces, eager and graph replay."""
     import torch.multiprocessing as mp
     mp.spawn(_worker, args=(2, _free_port(),
                             ["qwen3_small_kv", "llama_small_prompt", "qwen3_0p6b_kv512"]),
