@@ -532,6 +532,7 @@ def run_tp_decode(args, rank: int, world: int, dev) -> dict:
     ms_tok = measure("fused")
     ms_peer = measure("peer") if world > 1 else ms_tok
     ms_nccl = measure("nccl") if world > 1 else ms_tok
+    ar_us = allreduce_latency(world, dev, spec.hidden) if world > 1 else None
     wbytes = spec.int8_bytes_per_token()
     kvbytes = spec.kv_bytes_per_token(TP_CTX + TP_TOKENS // 2)
     peak, peak_kind = _peaks()
@@ -551,7 +552,45 @@ def run_tp_decode(args, rank: int, world: int, dev) -> dict:
             "with_peer_allreduce_kernel": {"us_per_token": round(ms_peer * 1e3, 1),
                                            "value": round(1.0 / (ms_peer * 1e-3), 1)},
             "with_nccl_allreduce": {"us_per_token": round(ms_nccl * 1e3, 1),
-                                    "value": round(1.0 / (ms_nccl * 1e-3), 1)}}
+                                    "value": round(1.0 / (ms_nccl * 1e-3), 1)},
+            "allreduce_us_per_call": ar_us}
+
+
+def allreduce_latency(world: int, dev, n: int) -> dict:
+    """Device time per all-reduce of n fp32 (one decode step's [H] partial):
+    200 back-to-back calls in one CUDA graph, max over ranks, for the
+    peer-memory kernel and for NCCL."""
+    import torch
+    import torch.distributed as dist
+    from quartz_b200.comm import PeerAllReduce
+    ar = PeerAllReduce(n, device=dev)
+    t = torch.randn(n, device=dev)
+    out = {}
+    for name, fn in (("peer_kernel", lambda: ar(t)), ("nccl", lambda: dist.all_reduce(t))):
+        for _ in range(5):
+            fn()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(g, stream=side):
+                for _ in range(200):
+                    fn()
+        torch.cuda.current_stream().wait_stream(side)
+        g.replay()
+        torch.cuda.synchronize()
+        _barrier(world)
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        out[name] = round(_dist_max(e0.elapsed_time(e1) * 1e3 / 200, world), 2)
+        del g              # a graph holding NCCL calls goes before the process group
+    ar.close()
+    return out
 
 
 def run_ours(args, rank: int, world: int, local: int) -> dict | None:
