@@ -143,6 +143,27 @@ int qz_fused_mlp_decode_noalloc(const int8_t* gu_q, const float* gu_s, int64_t n
  */
 int qz_silu_mul(const float* gu, float* a, int64_t M, int64_t I, void* stream);
 
+/*
+ * qz_gemv_w8 of RMSNorm(x) * norm_w (quartz/ops.py:24-32 followed by the
+ * projection, quartz/models/common.py:37-38): the streaming kernel normalises
+ * x as it stages it in shared memory (no separate launch). Shapes where the
+ * kernel keeps x in registers instead (K == 1024 and N > 36 * (SMs - 1), such
+ * as an lm_head) and shapes outside the streaming kernel
+ * normalise into xn_scratch ([K] device floats) first; NULL there makes such
+ * shapes return QZ_ERR_UNSUPPORTED.
+ */
+int qz_gemv_w8_rmsnorm(const int8_t* q, const float* scale, int64_t ng, const float* x,
+                       const float* norm_w, float eps, float* y, int64_t N, int64_t K,
+                       const float* residual, float* xn_scratch, void* stream);
+
+/* qz_fused_mlp_decode of RMSNorm(x) * norm_w, normalised in the kernel's
+ * activation staging; xn_scratch ([H]) as above. */
+int qz_fused_mlp_decode_rmsnorm(const int8_t* gu_q, const float* gu_s, int64_t ng,
+                                const float* x, const float* norm_w, float eps,
+                                const int8_t* down_q, const float* down_s, int64_t ngd,
+                                float* abuf, float* out, const float* residual, int64_t H,
+                                int64_t I, uint32_t* sync_ws, float* xn_scratch, void* stream);
+
 /* ------------------------------------------------------------------------
  * Decode-step glue: the fp32 work quartz's decoder does around its int8
  * matmuls, so a whole token can run on the device (and in one CUDA graph).

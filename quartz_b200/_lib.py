@@ -36,6 +36,10 @@ SIGNATURES = {
     "qz_fused_mlp_decode_noalloc": ([_vp, _vp, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64,
                                      _vp], _int),
     "qz_silu_mul": ([_vp, _vp, _i64, _i64, _vp], _int),
+    "qz_gemv_w8_rmsnorm": ([_vp, _vp, _i64, _vp, _vp, ctypes.c_float, _vp, _i64, _i64, _vp, _vp,
+                            _vp], _int),
+    "qz_fused_mlp_decode_rmsnorm": ([_vp, _vp, _i64, _vp, _vp, ctypes.c_float, _vp, _vp, _i64,
+                                     _vp, _vp, _vp, _i64, _i64, _vp, _vp, _vp], _int),
     "qz_embed_gather": ([_vp, _vp, _i64, _vp, _i64, _i64, _i64, _vp, _vp], _int),
     "qz_rmsnorm": ([_vp, _vp, _vp, _i64, _i64, ctypes.c_float, _vp], _int),
     "qz_qk_rope": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _int, _int, _int, _i64, _i64, _vp,

@@ -207,7 +207,14 @@ int launch_gemv(const DeviceInfo& d, const qz::GemvArgs& a, cudaStream_t st) {
 template <int R, bool PER_ROW>
 int launch_gemv_k(const DeviceInfo& d, const qz::GemvArgs& a, cudaStream_t st) {
   switch (kmode(a.K)) {
-    case qz::K1K: return launch_gemv<R, PER_ROW, qz::K1K>(d, a, st);
+    case qz::K1K:
+      // A folded RMSNorm needs x staged in shared memory (one coalesced pass
+      // per CTA). Single-row groups take the staged mode; four-row groups
+      // keep x in registers, where the extra 4 KB would cost a CTA per SM, so
+      // the caller runs the norm as its own pass.
+      if (a.norm_w && R == 1) return launch_gemv<R, PER_ROW, qz::KFULL>(d, a, st);
+      if (a.norm_w) return QZ_ERR_UNSUPPORTED;
+      return launch_gemv<R, PER_ROW, qz::K1K>(d, a, st);
     case qz::KFULL: return launch_gemv<R, PER_ROW, qz::KFULL>(d, a, st);
     default: return launch_gemv<R, PER_ROW, qz::KANY>(d, a, st);
   }
@@ -215,17 +222,20 @@ int launch_gemv_k(const DeviceInfo& d, const qz::GemvArgs& a, cudaStream_t st) {
 
 int gemv_impl(const int8_t* q, const float* scale, int64_t ng, const float* x, float* y,
               int64_t N, int64_t K, const float* residual, cudaStream_t st,
-              const qz::comm::PeerOut* po = nullptr) {
+              const qz::comm::PeerOut* po = nullptr, const float* norm_w = nullptr,
+              float eps = 0.f) {
   DeviceInfo* d = nullptr;
   if (int rc = device_info(&d)) return rc;
   const int64_t G = K / ng;
   const bool fits = qz::stream_smem_bytes(kTallRows, K) <= d->smem_optin - 256;
   const bool fast = K > 0 && K % 16 == 0 && G % 16 == 0 && aligned16(q) && fits;
-  if (!fast && po)
-    return fail(QZ_ERR_UNSUPPORTED, "qz_gemv_w8_peer: shape outside the streaming kernel");
+  if (!fast && (po || norm_w))
+    return fail(QZ_ERR_UNSUPPORTED, "gemv variant: shape outside the streaming kernel");
   if (!fast) return launch_generic_gemm(*d, q, scale, ng, x, y, residual, 1, N, K, st);
   qz::GemvArgs a{q, scale, x, y, residual, N, K, ng};
   if (po) a.po = *po;
+  a.norm_w = norm_w;
+  a.eps = eps;
   // Tall grouping unless it would leave SMs without a CTA.
   const bool tall = qz::cdiv(N, int64_t(kTallRows) * qz::kWarps) >= d->sms;
   if (ng == 1)
@@ -472,7 +482,7 @@ namespace {
 int mlp_impl(const int8_t* gu_q, const float* gu_s, int64_t ng, const float* x,
              const int8_t* down_q, const float* down_s, int64_t ngd, float* abuf, float* out,
              const float* residual, int64_t H, int64_t I, uint32_t* sync_ws, void* stream,
-             const qz::comm::PeerOut* po) {
+             const qz::comm::PeerOut* po, const float* norm_w = nullptr, float eps = 0.f) {
   if (int rc = check_weights(gu_q, gu_s, ng, 2 * I, H, "qz_fused_mlp_decode (gate|up)")) return rc;
   if (int rc = check_weights(down_q, down_s, ngd, H, I, "qz_fused_mlp_decode (down)")) return rc;
   if (H == 0) return QZ_OK;
@@ -486,8 +496,8 @@ int mlp_impl(const int8_t* gu_q, const float* gu_s, int64_t ng, const float* x,
   const bool fast = I > 0 && H % 16 == 0 && I % 16 == 0 && (H / ng) % 16 == 0 &&
                     (I / ngd) % 16 == 0 && aligned16(gu_q) && aligned16(down_q) && fits &&
                     sync_ws != nullptr && d->coop;
-  if (!fast && po)
-    return fail(QZ_ERR_UNSUPPORTED, "qz_fused_mlp_decode_peer: shape outside the fused kernel");
+  if (!fast && (po || norm_w))
+    return fail(QZ_ERR_UNSUPPORTED, "fused mlp variant: shape outside the fused kernel");
   if (!fast) {
     // Two launches: gate/up + SiLU into abuf, then the down GEMV.
     if (I > 0) {
@@ -500,6 +510,8 @@ int mlp_impl(const int8_t* gu_q, const float* gu_s, int64_t ng, const float* x,
   }
   qz::MlpArgs a{gu_q, gu_s, x, down_q, down_s, abuf, out, residual, sync_ws, H, I, ng, ngd};
   if (po) a.po = *po;
+  a.norm_w = norm_w;
+  a.eps = eps;
   const bool per_row = ng == 1 && ngd == 1;
   // Tall groups (2 units = 4 rows) unless too few units to fill the SMs.
   const bool tall = qz::cdiv(I, int64_t(kTallRows / 2) * qz::kWarps) >= d->sms;
@@ -543,6 +555,38 @@ int qz_fused_mlp_decode_peer(const int8_t* gu_q, const float* gu_s, int64_t ng, 
   if (int rc = peer_out(ps, H, &po, "qz_fused_mlp_decode_peer")) return rc;
   return mlp_impl(gu_q, gu_s, ng, x, down_q, down_s, ngd, abuf, nullptr, residual, H, I, sync_ws,
                   stream, &po);
+}
+
+int qz_gemv_w8_rmsnorm(const int8_t* q, const float* scale, int64_t ng, const float* x,
+                       const float* norm_w, float eps, float* y, int64_t N, int64_t K,
+                       const float* residual, float* xn_scratch, void* stream) {
+  if (int rc = check_weights(q, scale, ng, N, K, "qz_gemv_w8_rmsnorm")) return rc;
+  if (N == 0) return QZ_OK;
+  if (!y || !norm_w || (K > 0 && !x))
+    return fail(QZ_ERR_INVALID, "qz_gemv_w8_rmsnorm: null x, norm_w or y");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int rc = gemv_impl(q, scale, ng, x, y, N, K, residual, st, nullptr, norm_w, eps);
+  if (rc != QZ_ERR_UNSUPPORTED) return rc;
+  // other shapes: the norm into the caller's scratch, then the plain GEMV
+  if (!xn_scratch) return fail(QZ_ERR_UNSUPPORTED, "qz_gemv_w8_rmsnorm: shape needs xn_scratch");
+  if (int rc = qz_rmsnorm(x, norm_w, xn_scratch, 1, K, eps, stream)) return rc;
+  return gemv_impl(q, scale, ng, xn_scratch, y, N, K, residual, st);
+}
+
+int qz_fused_mlp_decode_rmsnorm(const int8_t* gu_q, const float* gu_s, int64_t ng,
+                                const float* x, const float* norm_w, float eps,
+                                const int8_t* down_q, const float* down_s, int64_t ngd,
+                                float* abuf, float* out, const float* residual, int64_t H,
+                                int64_t I, uint32_t* sync_ws, float* xn_scratch, void* stream) {
+  if (!norm_w) return fail(QZ_ERR_INVALID, "qz_fused_mlp_decode_rmsnorm: null norm_w");
+  const int rc = mlp_impl(gu_q, gu_s, ng, x, down_q, down_s, ngd, abuf, out, residual, H, I,
+                          sync_ws, stream, nullptr, norm_w, eps);
+  if (rc != QZ_ERR_UNSUPPORTED) return rc;
+  if (!xn_scratch)
+    return fail(QZ_ERR_UNSUPPORTED, "qz_fused_mlp_decode_rmsnorm: shape needs xn_scratch");
+  if (int rc2 = qz_rmsnorm(x, norm_w, xn_scratch, 1, H, eps, stream)) return rc2;
+  return mlp_impl(gu_q, gu_s, ng, xn_scratch, down_q, down_s, ngd, abuf, out, residual, H, I,
+                  sync_ws, stream, nullptr);
 }
 
 int qz_gemv_w8_peer(const int8_t* q, const float* scale, int64_t ng, const float* x, int64_t N,

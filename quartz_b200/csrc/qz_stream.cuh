@@ -61,6 +61,8 @@ struct GemvArgs {
   const float* residual;  // [N] or null
   int64_t N, K, ng;
   comm::PeerOut po;       // po.P > 0: push the rows to the ranks instead of writing y
+  const float* norm_w;    // non-null: the GEMV reads RMSNorm(x) * norm_w instead of x
+  float eps;
 };
 
 struct MlpArgs {
@@ -75,6 +77,8 @@ struct MlpArgs {
   unsigned int* sync_ws;  // grid barrier words {count, generation}, zero at first use
   int64_t H, I, ng, ngd;
   comm::PeerOut po;       // po.P > 0: push the rows to the ranks instead of writing out
+  const float* norm_w;    // non-null: phase 1 reads RMSNorm(x) * norm_w instead of x
+  float eps;
 };
 
 // ---------------------------------------------------------------------------
@@ -286,6 +290,39 @@ __device__ __forceinline__ void load_x_regs(const float* x, int lane, f2_t (&xr)
   }
 }
 
+// The norm weights are constants: a kernel prefetches the lines its threads
+// will read into L1 before it waits for the previous grid, so that applying
+// the norm costs no extra memory round trip after the sum of squares.
+__device__ __forceinline__ void prefetch_l1(const void* p) {
+  asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
+}
+
+// RMSNorm folded into the activation load (quartz/ops.py:24-32):
+// x <- x * (1 / sqrt(mean(x^2) + eps)) * w, on x staged in shared memory by
+// stage_x (K floats; any permutation of the staged layout sums the same
+// squares). Every thread of the CTA calls it after the staging barrier; it
+// ends with a barrier.
+__device__ __forceinline__ void norm_staged_x(float* xs, const float* __restrict__ w, int64_t K,
+                                              float eps, int tid, int nthr) {
+  __shared__ float red[32];
+  float ss = 0.f;
+  for (int64_t i = tid; i < K; i += nthr) ss = fmaf(xs[i], xs[i], ss);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  ss = 0.f;
+  for (int i = 0; i < (nthr >> 5); ++i) ss += red[i];
+  const float r = 1.0f / sqrtf(ss / static_cast<float>(K) + eps);
+  const int64_t nch = K / 16;
+  for (int64_t i = tid; i < K; i += nthr) {
+    const int64_t c = i >> 4, j = i & 15;
+    float& v = xs[((j >> 2) * nch + c) * 4 + (j & 3)];
+    v = v * r * w[i];
+  }
+  __syncthreads();
+}
+
 // Issue items [from, to) of a walk, one cp.async group each.
 template <int R, int KM, int D, class RowFn>
 __device__ __forceinline__ void issue_items(const Walk<R, D>& w, uint32_t ring, int64_t from,
@@ -358,11 +395,16 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_kernel(const GemvArgs a) 
     return row < r1 ? row : -1;
   };
   issue_item<R, KM>(w, ring_s, cursor_at(w, 0), lane, rowfn);
+  if constexpr (KM != K1K) {
+    if (a.norm_w)
+      for (int64_t i = tid * 32; i < a.K; i += kThreads * 32) prefetch_l1(a.norm_w + i);
+  }
   pdl_trigger();
   pdl_wait();
   if constexpr (KM != K1K) {
     stage_x(xs, a.x, a.K, tid, kThreads);
     __syncthreads();
+    if (a.norm_w) norm_staged_x(xs, a.norm_w, a.K, a.eps, tid, kThreads);
   }
 
   const int64_t G = a.K / a.ng;
@@ -461,9 +503,12 @@ __global__ void __launch_bounds__(kThreads, MINB) fused_mlp_kernel(const MlpArgs
   auto row2 = [&](int64_t g, int) -> int64_t { return h0 + g < h1 ? h0 + g : -1; };
 
   issue_item<R, KM1>(w1, ring_s, cursor_at(w1, 0), lane, row1);
+  if (a.norm_w)
+    for (int64_t i = tid * 32; i < H; i += kThreads * 32) prefetch_l1(a.norm_w + i);
   pdl_wait();
   stage_x(xs, a.x, H, tid, kThreads);
   __syncthreads();
+  if (a.norm_w) norm_staged_x(xs, a.norm_w, H, a.eps, tid, kThreads);
 
   // ---- phase 1 ----
   auto scale1 = [&](int64_t g, int r, int64_t grp) -> float {

@@ -15,6 +15,8 @@ only host traffic is the final token list.
 Differences of form (not of results) from quartz:
 * q, k and v are one stacked [(nq + 2 nkv) hd, H] int8 matrix (one GEMV
   instead of three; rows and scales are the three matrices' own);
+* the RMSNorms are applied by the kernels that consume them (the qkv GEMV,
+  the fused MLP, the lm_head GEMV normalise their input as they load it);
 * the KV cache is preallocated [layers, n_kv, max_ctx, head_dim] fp32 instead
   of growing in 256-position steps (quartz/cache.py:26-46);
 * prefill (M > 1) runs the tensor-core int8 GEMM and the causal prefill
@@ -121,7 +123,7 @@ class DecodeEngine:
 
     def __init__(self, spec: ModelSpec, int8_weights: Mapping | Iterable, norms: Mapping,
                  *, max_ctx: int, max_prefill: int = 512, device=None,
-                 persistent: bool = False):
+                 persistent: bool = False, fold_norms: bool = True):
         self.spec = spec
         self.dev = torch.device("cuda", qd.ensure_device(device))
         dev = self.dev
@@ -228,6 +230,7 @@ class DecodeEngine:
         self._graph = None
         self._graph_steps = 0
         self.trace = None   # set to a device uint64 tensor to record phase stamps
+        self.fold_norms = bool(fold_norms)   # RMSNorms inside the consuming kernels
         self.persistent = bool(persistent) and self._setup_persistent()
 
     def _setup_persistent(self) -> bool:
@@ -323,9 +326,15 @@ class DecodeEngine:
                                 p(self.tok), 1, S.vocab, H, h_a, st))
         for li, L in enumerate(self.layers):
             kc, vc = p(self.k_cache[li]), p(self.v_cache[li])
-            chk(lib.qz_rmsnorm(h_a, p(L.in_w), xn, 1, H, S.eps, st))
-            chk(lib.qz_gemv_w8(p(L.qkv_q), p(L.qkv_s), L.qkv_s.shape[1], xn, p(self.qkv),
-                               S.qkv_rows, H, None, st))
+            if self.fold_norms:
+                # the input RMSNorm happens inside the qkv GEMV's activation load
+                chk(lib.qz_gemv_w8_rmsnorm(p(L.qkv_q), p(L.qkv_s), L.qkv_s.shape[1], h_a,
+                                           p(L.in_w), S.eps, p(self.qkv), S.qkv_rows, H, None,
+                                           xn, st))
+            else:
+                chk(lib.qz_rmsnorm(h_a, p(L.in_w), xn, 1, H, S.eps, st))
+                chk(lib.qz_gemv_w8(p(L.qkv_q), p(L.qkv_s), L.qkv_s.shape[1], xn, p(self.qkv),
+                                   S.qkv_rows, H, None, st))
             chk(lib.qz_attention_decode_qkv(p(self.qkv), qd._ptr(L.qn_w), qd._ptr(L.kn_w),
                                             p(self.inv_freq), kc, vc, p(self.ao), nq, nkv, hd,
                                             self.max_ctx, 0, p(self.pos_dev), S.eps,
@@ -333,22 +342,45 @@ class DecodeEngine:
                                             self.attn_ws.numel(), st))
             chk(lib.qz_gemv_w8(p(L.o_q), p(L.o_s), L.o_s.shape[1], p(self.ao), h_b, H, nq * hd,
                                h_a, st))
-            chk(lib.qz_rmsnorm(h_b, p(L.post_w), xn, 1, H, S.eps, st))
-            chk(lib.qz_fused_mlp_decode(p(L.gu_q), p(L.gu_s), L.gu_s.shape[1], xn, p(L.down_q),
-                                        p(L.down_s), L.down_s.shape[1], p(self.abuf), h_a, h_b,
-                                        H, S.inter, p(self.mlp_ws), st))
-        chk(lib.qz_rmsnorm(h_a, p(self.norm_w), xn, 1, H, S.eps, st))
-        chk(lib.qz_gemv_w8(p(self.lm_q), p(self.lm_s), self.lm_s.shape[1], xn, p(self.logits),
-                           S.vocab, H, None, st))
+            if self.fold_norms:
+                # the post-attention RMSNorm happens inside the MLP's activation staging
+                chk(lib.qz_fused_mlp_decode_rmsnorm(p(L.gu_q), p(L.gu_s), L.gu_s.shape[1], h_b,
+                                                    p(L.post_w), S.eps, p(L.down_q),
+                                                    p(L.down_s), L.down_s.shape[1], p(self.abuf),
+                                                    h_a, h_b, H, S.inter, p(self.mlp_ws), xn, st))
+            else:
+                chk(lib.qz_rmsnorm(h_b, p(L.post_w), xn, 1, H, S.eps, st))
+                chk(lib.qz_fused_mlp_decode(p(L.gu_q), p(L.gu_s), L.gu_s.shape[1], xn,
+                                            p(L.down_q), p(L.down_s), L.down_s.shape[1],
+                                            p(self.abuf), h_a, h_b, H, S.inter, p(self.mlp_ws),
+                                            st))
+        if self.fold_norms:
+            chk(lib.qz_gemv_w8_rmsnorm(p(self.lm_q), p(self.lm_s), self.lm_s.shape[1], h_a,
+                                       p(self.norm_w), S.eps, p(self.logits), S.vocab, H, None,
+                                       xn, st))
+        else:
+            chk(lib.qz_rmsnorm(h_a, p(self.norm_w), xn, 1, H, S.eps, st))
+            chk(lib.qz_gemv_w8(p(self.lm_q), p(self.lm_s), self.lm_s.shape[1], xn,
+                               p(self.logits), S.vocab, H, None, st))
         chk(lib.qz_argmax(p(self.logits), 1, S.vocab, p(self.keys), p(self.tok), p(self.pos_dev),
                           1, st))
 
     def _launches_per_token(self) -> int:
         if self.persistent:
             return 4   # decode_layers, lm_head GEMV, argmax + finish
-        # embed + per layer (rmsnorm, qkv, attention, o, rmsnorm, mlp) + norm, lm, argmax x2;
-        # attention is one launch for the head shapes of the fused kernel
-        return 1 + 6 * self.spec.layers + 4
+        # embed + per layer (qkv with its norm, attention, o, mlp with its norm) + lm with
+        # the final norm, argmax x2; attention is one launch for the fused kernel's shapes;
+        # one more launch per norm when they are not folded. The library folds a norm
+        # into a GEMV unless it keeps x in registers (K = 1024 with four-row groups:
+        # more than 36 * (SMs - 1) rows), where the norm is a pass of its own.
+        S = self.spec
+        sms = torch.cuda.get_device_properties(self.dev).multi_processor_count
+
+        def norm_pass(n_rows: int, k: int) -> int:
+            return int(not self.fold_norms or (k == 1024 and n_rows > 36 * (sms - 1)))
+
+        per_layer = 4 + norm_pass(S.qkv_rows, S.hidden) + (0 if self.fold_norms else 1)
+        return 1 + per_layer * S.layers + 3 + norm_pass(S.vocab, S.hidden)
 
     def prefill(self, ids: Iterable[int]) -> int:
         """Run the prompt ids at the current position; return the greedy next token

@@ -93,8 +93,9 @@ def _ptr(t):
     return None if t is None else t.data_ptr()
 
 
-def gemv(q, scale, x, y=None, residual=None):
-    """y[n] = sum_g scale[n,g] sum_{j<G} x[gG+j] q[n,gG+j] (+ residual[n])."""
+def gemv(q, scale, x, y=None, residual=None, norm_w=None, eps=1e-6):
+    """y[n] = sum_g scale[n,g] sum_{j<G} x[gG+j] q[n,gG+j] (+ residual[n]).
+    With norm_w, the GEMV of RMSNorm(x) * norm_w (normalised in the kernel)."""
     N, K, ng = _weights(q, scale)
     ensure_device(q.device)
     _need(x, torch.float32, "x")
@@ -109,8 +110,17 @@ def gemv(q, scale, x, y=None, residual=None):
         _need(residual, torch.float32, "residual")
         if residual.numel() != N:
             raise ValueError("residual must have N elements")
-    _same_device(q.device, scale, x, y, residual)
+    _same_device(q.device, scale, x, y, residual, norm_w)
     with torch.cuda.device(q.device):
+        if norm_w is not None:
+            _need(norm_w, torch.float32, "norm_w", 1)
+            if norm_w.numel() != K:
+                raise ValueError("norm_w must have K elements")
+            scratch = torch.empty(K, dtype=torch.float32, device=q.device)
+            _lib.check(_lib.load().qz_gemv_w8_rmsnorm(
+                q.data_ptr(), scale.data_ptr(), ng, x.data_ptr(), norm_w.data_ptr(), float(eps),
+                y.data_ptr(), N, K, _ptr(residual), scratch.data_ptr(), _stream_ptr(q.device)))
+            return y
         _lib.check(_lib.load().qz_gemv_w8(q.data_ptr(), scale.data_ptr(), ng, x.data_ptr(),
                                           y.data_ptr(), N, K, _ptr(residual),
                                           _stream_ptr(q.device)))
@@ -175,8 +185,10 @@ def mlp_workspace(device) -> torch.Tensor:
     return ws
 
 
-def fused_mlp(gu_q, gu_s, x, down_q, down_s, abuf=None, out=None, residual=None):
-    """out = down(silu(gate.x) * (up.x)) (+ residual) for one token (M = 1)."""
+def fused_mlp(gu_q, gu_s, x, down_q, down_s, abuf=None, out=None, residual=None, norm_w=None,
+              eps=1e-6):
+    """out = down(silu(gate.x) * (up.x)) (+ residual) for one token (M = 1).
+    With norm_w, of RMSNorm(x) * norm_w (normalised in the kernel)."""
     I2, H = gu_q.shape
     _, _, ng = _weights(gu_q, gu_s, "gu_q")
     Hd, I, ngd = _weights(down_q, down_s, "down_q")
@@ -200,6 +212,17 @@ def fused_mlp(gu_q, gu_s, x, down_q, down_s, abuf=None, out=None, residual=None)
             raise ValueError("residual must have H elements")
     _same_device(dev, gu_s, x, down_q, down_s, abuf, out, residual)
     ws = mlp_workspace(dev)
+    if norm_w is not None:
+        _need(norm_w, torch.float32, "norm_w", 1)
+        if norm_w.numel() != H:
+            raise ValueError("norm_w must have H elements")
+        scratch = torch.empty(H, dtype=torch.float32, device=dev)
+        with torch.cuda.device(dev):
+            _lib.check(_lib.load().qz_fused_mlp_decode_rmsnorm(
+                gu_q.data_ptr(), gu_s.data_ptr(), ng, x.data_ptr(), norm_w.data_ptr(), float(eps),
+                down_q.data_ptr(), down_s.data_ptr(), ngd, abuf.data_ptr(), out.data_ptr(),
+                _ptr(residual), H, I, ws.data_ptr(), scratch.data_ptr(), _stream_ptr(dev)))
+        return out
     with torch.cuda.device(dev):
         _lib.check(_lib.load().qz_fused_mlp_decode(
             gu_q.data_ptr(), gu_s.data_ptr(), ng, x.data_ptr(), down_q.data_ptr(),

@@ -223,7 +223,7 @@ def _golden(cid, key):
         return z[f"{cid}__{key}"]
 
 
-def _engine(case, extra_ctx=0, persistent=False):
+def _engine(case, extra_ctx=0, persistent=False, fold_norms=True):
     from quartz_b200.decode import DecodeEngine
     from quartz_b200.model import ModelSpec, norm_weights, random_int8_weights
     spec = ModelSpec.from_hf(case["cfg"], case["arch"])
@@ -231,7 +231,7 @@ def _engine(case, extra_ctx=0, persistent=False):
     eng = DecodeEngine(spec, random_int8_weights(spec), norm_weights(spec),
                        max_ctx=start + case["steps"] + extra_ctx,
                        max_prefill=max(2, len(case.get("prompt", [])) or 2),
-                       persistent=persistent)
+                       persistent=persistent, fold_norms=fold_norms)
     return spec, eng
 
 
@@ -278,13 +278,15 @@ def test_engine_small(cuda_dev, cid, persistent):
     assert _run(case, eng, graph=True, unroll=5) == gold, "graph"
 
 
-@pytest.mark.parametrize("persistent", [True, False])
-def test_engine_qwen3_0p6b_kv512(cuda_dev, persistent):
+@pytest.mark.parametrize("persistent,fold_norms", [(True, True), (False, True), (False, False)])
+def test_engine_qwen3_0p6b_kv512(cuda_dev, persistent, fold_norms):
     """The all-int8 Qwen3-0.6B decode workload: 512 prefilled positions, 128
-    greedy tokens through the graph replay; the first step's top-8 logits too."""
+    greedy tokens through the graph replay; the first step's top-8 logits too.
+    Per-op engine with the RMSNorms folded into the GEMVs and as launches of
+    their own."""
     case = _cases()["qwen3_0p6b_kv512"]
     gold = _golden(case["id"], "tokens").tolist()
-    spec, eng = _engine(case, persistent=persistent)
+    spec, eng = _engine(case, persistent=persistent, fold_norms=fold_norms)
     assert eng.persistent == persistent
     from quartz_b200.model import seeded_kv
     eng.load_kv(seeded_kv(spec, case["kv_len"]))
@@ -307,3 +309,45 @@ def test_engine_llama_1b_prompt512(cuda_dev, persistent):
     _, eng = _engine(case, persistent=persistent)
     assert eng.persistent == persistent
     assert _run(case, eng, graph=True, unroll=16) == gold
+
+
+@pytest.mark.parametrize("N,K,ng,w_off", [(4096, 1024, 1, 0), (3072, 2048, 1, 0),
+                                          (1024, 3072, 1, 0), (500, 100, 1, 0),
+                                          (2048, 1024, 8, 0), (8192, 1024, 1, 0),
+                                          (6000, 1024, 4, 0), (8192, 1024, 1, 1)])
+def test_gemv_with_folded_rmsnorm(cuda_dev, N, K, ng, w_off):
+    """The GEMV of RMSNorm(x) * w with the norm inside the kernel's activation
+    load against the two steps in fp64: single-row groups stage x in shared
+    memory (any alignment of the norm weights, w_off = 1 float); four-row
+    groups at K = 1024 (N > 5292 on 148 SMs) and shapes outside the streaming
+    kernel go through the scratch path."""
+    from quartz_b200 import device as qd
+    g = torch.Generator().manual_seed(N + K)
+    q = torch.randint(-127, 128, (N, K), generator=g, dtype=torch.int8).to(cuda_dev)
+    s = (torch.rand(N, ng, generator=g) * 1e-3 + 1e-4).to(cuda_dev)
+    x = (torch.randn(K, generator=g) * 3).to(cuda_dev)
+    w = (1 + 0.1 * torch.randn(K + w_off, generator=g)).to(cuda_dev)[w_off:]
+    res = torch.randn(N, generator=g).to(cuda_dev)
+    xn = _rms_ref(x, w, 1e-6).double()
+    wd = (q.double().view(N, ng, K // ng) * s.double()[:, :, None]).view(N, K)
+    ref = wd @ xn + res.double()
+    _close(qd.gemv(q, s, x, residual=res, norm_w=w), ref, f"gemv+norm {N}x{K}")
+
+
+@pytest.mark.parametrize("H,I", [(1024, 3072), (2048, 8192), (4096, 1536)])
+def test_fused_mlp_with_folded_rmsnorm(cuda_dev, H, I):
+    from quartz_b200 import device as qd
+    g = torch.Generator().manual_seed(H + I)
+    gu = torch.randint(-127, 128, (2 * I, H), generator=g, dtype=torch.int8).to(cuda_dev)
+    gus = (torch.rand(2 * I, 1, generator=g) * 2e-4 + 1e-4).to(cuda_dev)
+    dq = torch.randint(-127, 128, (H, I), generator=g, dtype=torch.int8).to(cuda_dev)
+    ds = (torch.rand(H, 1, generator=g) * 2e-4 + 1e-4).to(cuda_dev)
+    x = (torch.randn(H, generator=g) * 2).to(cuda_dev)
+    w = (1 + 0.1 * torch.randn(H, generator=g)).to(cuda_dev)
+    res = torch.randn(H, generator=g).to(cuda_dev)
+    xn = _rms_ref(x, w, 1e-6).double()
+    a = (gu.double() * gus.double()) @ xn
+    gate, up = a[:I], a[I:]
+    act = gate / (1 + torch.exp(-gate)) * up
+    ref = (dq.double() * ds.double()) @ act + res.double()
+    _close(qd.fused_mlp(gu, gus, x, dq, ds, residual=res, norm_w=w), ref, f"mlp+norm {H}x{I}")
