@@ -775,10 +775,19 @@ template <int E, int NR, bool QKV>
 int launch_attn_fused(const qz::dec::AttnArgs& a, int S, cudaStream_t st) {
   constexpr int smem = qz::dec::attn_fused_smem<E, NR>();
   static_assert(smem <= 48 * 1024, "fused attention shared memory above the default limit");
-  qz::dec::attn_decode_fused_kernel<E, NR, QKV>
-      <<<dim3(static_cast<unsigned>(a.nkv), static_cast<unsigned>(S)), qz::dec::kAttnThreads,
-         smem, st>>>(a);
-  QZ_CUDA(cudaGetLastError());
+  // a programmatic dependent launch: the kernel hints its cache rows into L2
+  // before griddepcontrol.wait and lets the next kernel launch early
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(static_cast<unsigned>(a.nkv), static_cast<unsigned>(S));
+  cfg.blockDim = dim3(qz::dec::kAttnThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  QZ_CUDA(cudaLaunchKernelEx(&cfg, qz::dec::attn_decode_fused_kernel<E, NR, QKV>, a));
   return QZ_OK;
 }
 

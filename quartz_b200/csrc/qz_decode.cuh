@@ -601,6 +601,27 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_fused_kernel(AttnArg
   __shared__ unsigned s_last;
   const int g = blockIdx.x, c = blockIdx.y, S = gridDim.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t kv_off = static_cast<int64_t>(g) * a.max_ctx * HD;
+  // Launched as a programmatic dependent of the projection that writes `in`:
+  // the next kernel may launch now (it waits for this grid's completion),
+  // and before waiting for the previous grid this CTA only hints the cache
+  // rows it will read into L2. The context length read here can be stale;
+  // the rows are clamped inside the cache, and everything after the wait
+  // reads it again.
+  pdl_trigger();
+  {
+    int64_t Tp = (a.len_dev ? *a.len_dev : a.len0) + a.len_off;
+    Tp = Tp > a.max_ctx ? a.max_ctx : (Tp < 0 ? 0 : Tp);
+    const int64_t per_p = Tp > 0 ? (cdiv(Tp, S) + 7) / 8 * 8 : 0;
+    const int64_t p0 = static_cast<int64_t>(c) * per_p, p1 = min64(Tp, p0 + per_p);
+    constexpr int kLines = HD * 4 / 128;   // 128-byte lines per cache row
+    for (int64_t i = threadIdx.x; i < (p1 - p0) * 2 * kLines; i += kAttnThreads) {
+      const int64_t t = p0 + i / (2 * kLines);
+      const int j = static_cast<int>(i % (2 * kLines));
+      prefetch_l2((j < kLines ? a.kc : a.vc) + kv_off + t * HD + (j % kLines) * 32);
+    }
+  }
+  pdl_wait();
   int64_t T = (a.len_dev ? *a.len_dev : a.len0) + a.len_off;
   T = T > a.max_ctx ? a.max_ctx : T;
   const int64_t per = T > 0 ? (cdiv(T, S) + 7) / 8 * 8 : 0;
@@ -611,7 +632,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_fused_kernel(AttnArg
   const int64_t t_raw = (a.len_dev ? *a.len_dev : a.len0) + a.len_off;
   const bool append = QKV && t_raw >= 1 && t_raw <= a.max_ctx;
   float* pbase = a.part + (static_cast<int64_t>(g) * S + c) * NR * (HD + 2);
-  const int64_t kv_off = static_cast<int64_t>(g) * a.max_ctx * HD;
 
   if (t0 < t1) {
     // queries of this group (and, in the owning CTA, the new key/value)

@@ -296,6 +296,9 @@ __device__ __forceinline__ void load_x_regs(const float* x, int lane, f2_t (&xr)
 __device__ __forceinline__ void prefetch_l1(const void* p) {
   asm volatile("prefetch.global.L1 [%0];" ::"l"(p));
 }
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(p));
+}
 
 // RMSNorm folded into the activation load (quartz/ops.py:24-32):
 // x <- x * (1 / sqrt(mean(x^2) + eps)) * w, on x staged in shared memory by
@@ -333,7 +336,8 @@ __device__ __forceinline__ void issue_items(const Walk<R, D>& w, uint32_t ring, 
 
 // One walk through a ring of D slots. Before the call, the positions of items
 // 0 .. D-2 have been issued (committed as one group each, empty groups for
-// missing items). Each step issues the item D-1 ahead (past the end:
+// missing items), and item D-1 as well when `ahead_issued` (the whole ring;
+// the first step then issues nothing). Each step issues the item D-1 ahead (past the end:
 // `beyond()` issues the next walk's item or an empty group), waits for the
 // current item and accumulates it; at a group's last segment `done(g, sum)`
 // runs on every lane (sum is meaningful on the lanes reduced_row<R>() names).
@@ -344,7 +348,7 @@ template <int R, bool PER_ROW, int KM, int D, class RowFn, class ScaleFn, class 
 __device__ __forceinline__ void walk(const Walk<R, D>& w, uint32_t ring_s, const uint8_t* ring,
                                      const uint8_t* xs, const float* xg, int lane, int64_t G,
                                      RowFn rowfn, ScaleFn scale_of, BeyondFn beyond,
-                                     DoneFn done) {
+                                     DoneFn done, bool ahead_issued = false) {
   f2_t xr[2][8];
   if constexpr (KM == K1K) load_x_regs(xg, lane, xr);
   f2_t acc[R];
@@ -352,7 +356,9 @@ __device__ __forceinline__ void walk(const Walk<R, D>& w, uint32_t ring_s, const
   Cursor<D> cur = cursor_at(w, 0);
   Cursor<D> ahead = cursor_at(w, D - 1);
   for (; cur.g < w.ngrp; cur.next(w.nseg), ahead.next(w.nseg)) {
-    if (ahead.g < w.ngrp)
+    if (ahead_issued)
+      ahead_issued = false;     // the caller already issued item D-1
+    else if (ahead.g < w.ngrp)
       issue_item<R, KM>(w, ring_s, ahead, lane, rowfn);
     else
       beyond();
@@ -394,7 +400,10 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_kernel(const GemvArgs a) 
     const int64_t row = r0 + g * R + r;
     return row < r1 ? row : -1;
   };
+  // The weights do not depend on the previous grid: fill the whole ring
+  // before waiting for it.
   issue_item<R, KM>(w, ring_s, cursor_at(w, 0), lane, rowfn);
+  issue_item<R, KM>(w, ring_s, cursor_at(w, kDepth - 1), lane, rowfn);
   if constexpr (KM != K1K) {
     if (a.norm_w)
       for (int64_t i = tid * 32; i < a.K; i += kThreads * 32) prefetch_l1(a.norm_w + i);
@@ -432,7 +441,7 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_kernel(const GemvArgs a) 
   };
   auto beyond = [&]() { cp_async_commit(); };
   walk<R, PER_ROW, KM>(w, ring_s, ring, reinterpret_cast<const uint8_t*>(xs), a.x, lane, G, rowfn,
-                       scale_of, beyond, done);
+                       scale_of, beyond, done, true);
   cp_async_wait<0>();
 }
 
