@@ -60,6 +60,18 @@ int qz_gemv_w8(const int8_t* q, const float* scale, int64_t ng, const float* x, 
                int64_t N, int64_t K, const float* residual, void* stream);
 
 /*
+ * The whole numpy-signature call of w8a32_gemv (quartz/kernels/int8.py:24-38:
+ * x and y in host memory, y complete on return) in one call: x_host is
+ * copied into x_pin (pinned, K floats) and on to x_dev, the GEMV writes y_dev,
+ * and y comes back through y_pin (pinned, N floats) into y_host in chunks, the
+ * host copy of one chunk overlapping the transfer of the next. q and scale
+ * are device pointers. Synchronises with the stream; allocates nothing.
+ */
+int qz_gemv_w8_host(const int8_t* q, const float* scale, int64_t ng, const float* x_host,
+                    float* y_host, int64_t N, int64_t K, float* x_pin, float* y_pin,
+                    float* x_dev, float* y_dev, void* stream);
+
+/*
  * Y[m, n] = the same reduction for each of M rows of X [M, K]  (+ residual[m, n])
  * Replaces w8a32_gemm (quartz/kernels/int8.py:66-87). Y is [M, N]; residual,
  * if not NULL, is [M, N]. M == 1 runs the GEMV.

@@ -68,10 +68,12 @@ class _Staging:
     def __init__(self, dev: int):
         self.dev = dev
         self.bufs: dict[str, torch.Tensor] = {}
+        self.io = None
 
     def get(self, name: str, nbytes: int, pinned: bool) -> torch.Tensor:
         b = self.bufs.get(name)
         if b is None or b.numel() < nbytes:
+            self.io = None   # cached raw pointers may name the buffer being replaced
             n = max(nbytes, 4096)
             if pinned:
                 b = torch.empty(n, dtype=torch.uint8, pin_memory=True)
@@ -89,6 +91,22 @@ def staging(dev: int) -> _Staging:
     if s is None:
         s = _staging[dev] = _Staging(dev)
     return s
+
+
+def io_ptrs(dev: int, x_bytes: int, y_bytes: int) -> tuple[int, int, int, int]:
+    """Raw pointers (pinned x, pinned y, device x, device y) of the GEMV's
+    staging buffers with at least these sizes; cached while they fit."""
+    st = staging(dev)
+    p = getattr(st, "io", None)
+    if p is not None and p[0] >= x_bytes and p[1] >= y_bytes:
+        return p[2]
+    xb, yb = max(x_bytes, 4096), max(y_bytes, 4096)
+    bufs = (st.get("x.h", xb, pinned=True), st.get("y.h", yb, pinned=True),
+            st.get("x.d", xb, pinned=False), st.get("y.d", yb, pinned=False))
+    ptrs = tuple(b.data_ptr() for b in bufs)
+    st.io = (min(b.numel() for b in (bufs[0], bufs[2])),
+             min(b.numel() for b in (bufs[1], bufs[3])), ptrs)
+    return ptrs
 
 
 def to_device(a: np.ndarray, name: str, dev: int) -> torch.Tensor:

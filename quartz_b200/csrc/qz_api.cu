@@ -432,6 +432,61 @@ int qz_gemv_w8(const int8_t* q, const float* scale, int64_t ng, const float* x, 
   return gemv_impl(q, scale, ng, x, y, N, K, residual, static_cast<cudaStream_t>(stream));
 }
 
+namespace {
+// Device-to-host copies of y go out in chunks of this size, each followed by
+// an event, so the host copy of one chunk into the caller's array overlaps
+// the DMA of the next.
+constexpr int64_t kHostChunkBytes = 128 * 1024;
+constexpr int kHostChunks = 16;
+thread_local cudaEvent_t t_copy_ev[kMaxDevices][kHostChunks];
+
+int copy_events(cudaEvent_t** out) {
+  int dev = 0;
+  QZ_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(QZ_ERR_UNSUPPORTED, "device index out of range");
+  cudaEvent_t* ev = t_copy_ev[dev];
+  if (!ev[0])
+    for (int i = 0; i < kHostChunks; ++i)
+      QZ_CUDA(cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming));
+  *out = ev;
+  return QZ_OK;
+}
+}  // namespace
+
+int qz_gemv_w8_host(const int8_t* q, const float* scale, int64_t ng, const float* x_host,
+                    float* y_host, int64_t N, int64_t K, float* x_pin, float* y_pin,
+                    float* x_dev, float* y_dev, void* stream) {
+  if (int rc = check_weights(q, scale, ng, N, K, "qz_gemv_w8_host")) return rc;
+  if (N == 0) return QZ_OK;
+  if (!y_host || !y_pin || !y_dev || (K > 0 && (!x_host || !x_pin || !x_dev)))
+    return fail(QZ_ERR_INVALID, "qz_gemv_w8_host: null host, pinned or device buffer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaEvent_t* ev = nullptr;
+  if (int rc = copy_events(&ev)) return rc;
+  if (K > 0) {
+    std::memcpy(x_pin, x_host, static_cast<size_t>(K) * 4);
+    QZ_CUDA(cudaMemcpyAsync(x_dev, x_pin, static_cast<size_t>(K) * 4, cudaMemcpyHostToDevice, st));
+  }
+  if (int rc = gemv_impl(q, scale, ng, x_dev, y_dev, N, K, nullptr, st)) return rc;
+  const int64_t bytes = N * 4;
+  const int64_t chunk = std::max<int64_t>(kHostChunkBytes, qz::cdiv(bytes, kHostChunks * 16) * 16);
+  const int n = static_cast<int>(qz::cdiv(bytes, chunk));
+  for (int i = 0; i < n; ++i) {
+    const int64_t off = i * chunk, len = std::min(chunk, bytes - off);
+    QZ_CUDA(cudaMemcpyAsync(reinterpret_cast<char*>(y_pin) + off,
+                            reinterpret_cast<const char*>(y_dev) + off, static_cast<size_t>(len),
+                            cudaMemcpyDeviceToHost, st));
+    QZ_CUDA(cudaEventRecord(ev[i], st));
+  }
+  for (int i = 0; i < n; ++i) {
+    const int64_t off = i * chunk, len = std::min(chunk, bytes - off);
+    QZ_CUDA(cudaEventSynchronize(ev[i]));
+    std::memcpy(reinterpret_cast<char*>(y_host) + off, reinterpret_cast<const char*>(y_pin) + off,
+                static_cast<size_t>(len));
+  }
+  return QZ_OK;
+}
+
 int qz_gemm_w8(const int8_t* q, const float* scale, int64_t ng, const float* X, float* Y,
                int64_t M, int64_t N, int64_t K, const float* residual, void* stream) {
   if (int rc = check_weights(q, scale, ng, N, K, "qz_gemm_w8")) return rc;

@@ -15,7 +15,7 @@ from __future__ import annotations
 import numpy as np
 import torch
 
-from .. import _host
+from .. import _host, _lib
 from .. import device as _dev
 
 # The reference routes int8 GEMVs below this many weight bytes to a serial
@@ -67,10 +67,14 @@ def w8a32_gemv(q, scale, x, y) -> None:
     _check_out(y, (N,), "y")
     d = _dev_index()
     qd, sd = _host.resident(q, d), _host.resident(scale, d)
-    xd = _host.to_device(x, "x", d)
-    yd = _host.out_buffer((N,), "y", d)
-    _dev.gemv(qd, sd, xd, yd)
-    _host.to_host(yd, y, "y")
+    if x.dtype != np.float32 or not x.flags["C_CONTIGUOUS"]:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+    # one library call: x in through pinned memory, the GEMV, y back in chunks
+    xp, yp, xdv, ydv = _host.io_ptrs(d, 4 * K, 4 * N)
+    _lib.check(_lib.load().qz_gemv_w8_host(
+        qd.data_ptr(), sd.data_ptr(), scale.shape[1], x.__array_interface__["data"][0],
+        y.__array_interface__["data"][0], N, K, xp, yp, xdv, ydv,
+        torch.cuda.current_stream(d).cuda_stream))
 
 
 def w8a32_gemv_serial(q, scale, x, y) -> None:
