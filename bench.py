@@ -185,6 +185,74 @@ def run_reference(args) -> dict:
 # ---------------------------------------------------------------------------
 # GPU side
 # ---------------------------------------------------------------------------
+def run_gemv_int4(args, dev, world: int = 1) -> dict:
+    """The lm_head GEMV on int4 weights (two per byte, per-row scale; quartz has
+    no 4-bit kernel, so this line has no reference arm): the same Qwen3-0.6B
+    lm_head shape and x as the headline, weights quantised from the same fp32
+    draw, 3 rotating copies of 77.8 MB (> L2) in one CUDA graph."""
+    import torch
+    from quartz_b200 import device as qdev
+    from quartz_b200.quantize import quantize_symmetric_int4
+    import oracle
+
+    N, K = LM_HEAD_N, LM_HEAD_K
+    rng = np.random.default_rng(0)
+    W = rng.standard_normal((N, K), dtype=np.float32) * np.float32(0.02)
+    q4, s4 = quantize_symmetric_int4(W, None)
+    del W
+    x = rng.standard_normal(K, dtype=np.float32)
+    copies = 3
+    qs = [torch.from_numpy(q4).to(dev) for _ in range(copies)]
+    sd = torch.from_numpy(s4).to(dev)
+    xd = torch.from_numpy(x).to(dev)
+    ys = [torch.empty(N, dtype=torch.float32, device=dev) for _ in range(copies)]
+    qdev.gemv_w4(qs[0], sd, xd, ys[0])
+    torch.cuda.synchronize()
+    ref = np.empty(N, np.float32)
+    oracle.w4a32_gemv(q4, s4, x, ref)
+    rel = float(np.abs(ys[0].cpu().numpy() - ref).max() / np.abs(ref).max())
+    if rel > 1e-4:
+        raise SystemExit(f"int4 GEMV parity failed: rel err {rel:.3e}")
+    chunk = 240
+    stream = torch.cuda.current_stream()
+    side = torch.cuda.Stream()
+    side.wait_stream(stream)
+    with torch.cuda.stream(side):
+        qdev.gemv_w4(qs[1], sd, xd, ys[1])
+    stream.wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(chunk):
+            qdev.gemv_w4(qs[i % copies], sd, xd, ys[i % copies])
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    reps = max(2, args.steps // (chunk * 2))
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    _barrier(world)
+    e0.record(stream)
+    for _ in range(reps):
+        g.replay()
+    e1.record(stream)
+    _barrier(world)
+    qdev.check_status(dev)
+    ms = _dist_max(e0.elapsed_time(e1) / (reps * chunk), world)
+    nbytes = N * K // 2 + 4 * N + 4 * K + 4 * N
+    peak, peak_kind = _peaks()
+    achieved = nbytes / (ms * 1e-3) / 1e9
+    del g
+    return {"workload": "qwen3-0.6b lm_head GEMV [151936x1024] on int4 weights (packed two per "
+                        "byte, per-row scale), M=1", "value": round(world * achieved, 1),
+            "unit": UNIT, "us_per_gemv": round(ms * 1e3, 3), "steps": reps * chunk,
+            "bytes_per_gemv": nbytes, "weights_per_s": round(N * K / (ms * 1e-3), 1),
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": UNIT, "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "per": "one GPU"},
+            "gpu_launches": reps * chunk}
+
+
 def run_mlp_body(args, dev, world: int = 1, do_cpu: bool = True) -> dict:
     """Fused int8 MLP body at Qwen3-0.6B shape, M = 1: one step runs the 28
     independently seeded layers (seed 1000 + l) back to back, each on its own
@@ -709,6 +777,8 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     if not args.no_mlp:
         mlp = run_mlp_body(args, dev, world=world, do_cpu=(world == 1 and not args.no_cpu))
     _log(rank, "mlp body done")
+    w4 = None if args.no_int4 else run_gemv_int4(args, dev, world=world)
+    _log(rank, "int4 GEMV done")
     dec = None if args.no_decode else run_decode(args, dev, world=world)
     _log(rank, "decode done")
     tp = None if args.no_tp else run_tp(args, rank, world, dev)
@@ -741,7 +811,7 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
         "cpu_baseline": cpu,
         "clocks": clk.summary() if clk else None,
         "gpu_launches": args.steps,
-        "secondary": {"mlp_body": mlp, "decode": dec, "tensor_parallel": tp},
+        "secondary": {"mlp_body": mlp, "gemv_int4": w4, "decode": dec, "tensor_parallel": tp},
     }
 
 
@@ -758,6 +828,7 @@ def main():
     ap.add_argument("--no-mlp", action="store_true")
     ap.add_argument("--no-tp", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
+    ap.add_argument("--no-int4", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=500)
     ap.add_argument("--cpu-reps", type=int, default=30)
     args = ap.parse_args()

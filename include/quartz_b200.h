@@ -72,6 +72,19 @@ int qz_gemv_w8_host(const int8_t* q, const float* scale, int64_t ng, const float
                     float* x_dev, float* y_dev, void* stream);
 
 /*
+ * int4 weight GEMV: y[n] = sum_g scale[n, g] * sum_{j < G} x[g*G + j] * q[n, g*G + j]
+ * (+ residual[n]) with q stored two weights per byte, q4 [N, K / 2]: element
+ * 2i in the low nibble, 2i + 1 in the high one, two's complement, symmetric
+ * in [-7, 7] (quartz_b200.quantize.quantize_symmetric_int4). No counterpart
+ * in the reference: quartz keeps a `bits` field for 4-bit weights as future
+ * work (quartz/config.py:98). K and the group size G = K / ng must be
+ * multiples of 32 and q4 16-byte aligned; other shapes return
+ * QZ_ERR_INVALID. residual may be NULL.
+ */
+int qz_gemv_w4(const uint8_t* q4, const float* scale, int64_t ng, const float* x, float* y,
+               int64_t N, int64_t K, const float* residual, void* stream);
+
+/*
  * Y[m, n] = the same reduction for each of M rows of X [M, K]  (+ residual[m, n])
  * Replaces w8a32_gemm (quartz/kernels/int8.py:66-87). Y is [M, N]; residual,
  * if not NULL, is [M, N]. M == 1 runs the GEMV.

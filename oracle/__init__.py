@@ -9,6 +9,7 @@ from .oracle import (  # noqa: F401
     threads,
     set_threads,
     w8a32_gemv,
+    w4a32_gemv,
     w8a32_gemv_serial,
     w8a32_gemm,
     matmul_int8,

@@ -10,6 +10,9 @@ TEST INFRASTRUCTURE ONLY -- the checker and the CPU baseline, never the product.
   (flatten to [M, K], K % ng check, M == 1 -> GEMV, else GEMM).
 * ``mlp_per_op`` restates the M > 1 FusedMLP fallback quartz/quantize.py:112-114
   with the clipped silu of quartz/ops.py:35-37.
+* ``w4a32_gemv`` is the int4 GEMV in numpy: the int8 GEMV's group sums on
+  weights unpacked from two-per-byte nibbles. quartz has no 4-bit kernel, so
+  this one is pinned to nothing but its own definition (parity unpinned).
 """
 
 from __future__ import annotations
@@ -126,6 +129,25 @@ def matmul_int8(q, scale, x):
     else:
         w8a32_gemm(q, scale, xm, y)
     return y.reshape(*lead, N)
+
+
+def w4a32_gemv(q4, scale, x, y) -> None:
+    """int4 GEMV restated in numpy (no reference counterpart: quartz keeps
+    4-bit weights as future work, quartz/config.py:98). q4 (N, K/2) uint8,
+    element 2i in the low nibble of byte i, 2i+1 in the high one, two's
+    complement; y[n] = sum_g scale[n,g] * sum_j f32(q[n, gG+j]) x[gG+j], the
+    group sums of int8.py:24-38, accumulated in float64 and rounded once."""
+    q4 = np.asarray(q4, dtype=np.uint8)
+    lo = (q4 & 0x0F).astype(np.int16)
+    hi = (q4 >> 4).astype(np.int16)
+    q = np.empty(q4.shape[:-1] + (2 * q4.shape[-1],), np.int16)
+    q[..., 0::2] = np.where(lo > 7, lo - 16, lo)
+    q[..., 1::2] = np.where(hi > 7, hi - 16, hi)
+    N, K = q.shape
+    ng = scale.shape[1]
+    G = K // ng
+    part = (q.reshape(N, ng, G).astype(np.float64) * np.asarray(x, np.float64).reshape(1, ng, G)).sum(-1)
+    y[...] = (part * scale.astype(np.float64)).sum(-1).astype(np.float32)
 
 
 def fused_mlp_decode(gu_q, gu_s, x, down_q, down_s, abuf, out) -> None:

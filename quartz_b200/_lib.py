@@ -26,6 +26,7 @@ SIGNATURES = {
     "qz_init": ([_int], _int),
     "qz_last_error": ([ctypes.c_char_p, ctypes.c_size_t], _int),
     "qz_gemv_w8": ([_vp, _vp, _i64, _vp, _vp, _i64, _i64, _vp, _vp], _int),
+    "qz_gemv_w4": ([_vp, _vp, _i64, _vp, _vp, _i64, _i64, _vp, _vp], _int),
     "qz_gemv_w8_host": ([_vp, _vp, _i64, _vp, _vp, _i64, _i64, _vp, _vp, _vp, _vp, _vp], _int),
     "qz_gemm_w8": ([_vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _vp, _vp], _int),
     "qz_fused_mlp_decode": ([_vp, _vp, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _vp, _i64, _i64,

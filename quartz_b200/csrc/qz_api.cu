@@ -69,6 +69,19 @@ cudaError_t allow_gemv_variants(int smem) {
   return e;
 }
 
+template <int R, bool ANY>
+cudaError_t allow_gemv_w4_variants(int smem) {
+  cudaError_t e = cudaSuccess;
+  auto set = [&](auto fn) { if (e == cudaSuccess) e = allow_smem(fn, smem); };
+  set(qz::gemv_w4_kernel<R, true, qz::KFULL, kMinBlocks>);
+  set(qz::gemv_w4_kernel<R, false, qz::KFULL, kMinBlocks>);
+  if constexpr (ANY) {
+    set(qz::gemv_w4_kernel<R, true, qz::KANY, kMinBlocks>);
+    set(qz::gemv_w4_kernel<R, false, qz::KANY, kMinBlocks>);
+  }
+  return e;
+}
+
 template <int R>
 cudaError_t allow_mlp_variants(int smem) {
   cudaError_t e = cudaSuccess;
@@ -107,6 +120,8 @@ int device_info(DeviceInfo** out) {
       const int smem = d.smem_optin - 256;
       QZ_CUDA(allow_gemv_variants<kTallRows>(smem));
       QZ_CUDA(allow_gemv_variants<1>(smem));
+      QZ_CUDA((allow_gemv_w4_variants<2 * kTallRows, false>(smem)));
+      QZ_CUDA((allow_gemv_w4_variants<2, true>(smem)));
       QZ_CUDA(allow_mlp_variants<kTallRows>(smem));
       QZ_CUDA(allow_mlp_variants<2>(smem));
       d.ready = true;
@@ -218,6 +233,27 @@ int launch_gemv_k(const DeviceInfo& d, const qz::GemvArgs& a, cudaStream_t st) {
     case qz::KFULL: return launch_gemv<R, PER_ROW, qz::KFULL>(d, a, st);
     default: return launch_gemv<R, PER_ROW, qz::KANY>(d, a, st);
   }
+}
+
+// int4 row groups: twice the int8 kernel's rows per item over half-size
+// (512-byte) segments, so an item carries the same bytes.
+constexpr int kW4TallRows = 2 * kTallRows;
+constexpr int kW4Rows = 2;
+
+int w4_smem_bytes(int R, int64_t K) {
+  return qz::w4_x_bytes(K) + qz::kWarps * qz::kDepth * R * qz::kW4Seg;
+}
+
+template <int R, bool PER_ROW, int KM>
+int launch_gemv_w4(const DeviceInfo& d, const qz::GemvArgs& a, cudaStream_t st) {
+  auto fn = qz::gemv_w4_kernel<R, PER_ROW, KM, kMinBlocks>;
+  const int smem = w4_smem_bytes(R, a.K);
+  int nb = 0;
+  if (int rc = blocks_per_sm(fn, smem, &nb)) return rc;
+  if (nb < 1) return fail(QZ_ERR_UNSUPPORTED, "qz_gemv_w4: shared memory does not fit");
+  const int64_t want = qz::cdiv(a.N, int64_t(R) * qz::kWarps);
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(want, int64_t(d.sms) * nb)));
+  return launch_ex(fn, grid, smem, st, false, a);
 }
 
 int gemv_impl(const int8_t* q, const float* scale, int64_t ng, const float* x, float* y,
@@ -485,6 +521,38 @@ int qz_gemv_w8_host(const int8_t* q, const float* scale, int64_t ng, const float
                 static_cast<size_t>(len));
   }
   return QZ_OK;
+}
+
+
+int qz_gemv_w4(const uint8_t* q4, const float* scale, int64_t ng, const float* x, float* y,
+               int64_t N, int64_t K, const float* residual, void* stream) {
+  if (N < 0 || K < 0) return fail(QZ_ERR_INVALID, "qz_gemv_w4: negative dimension");
+  if (ng < 1 || K % ng != 0) return fail(QZ_ERR_INVALID, "qz_gemv_w4: ng must be >= 1 and divide K");
+  if (K % 32 != 0 || (K / ng) % 32 != 0)
+    return fail(QZ_ERR_INVALID, "qz_gemv_w4: K and the group size must be multiples of 32");
+  if (N == 0) return QZ_OK;
+  if (K == 0) return fail(QZ_ERR_INVALID, "qz_gemv_w4: K must be positive");
+  if (!q4 || !scale || !x || !y) return fail(QZ_ERR_INVALID, "qz_gemv_w4: null pointer");
+  if (!aligned16(q4)) return fail(QZ_ERR_INVALID, "qz_gemv_w4: q4 must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  if (w4_smem_bytes(kW4TallRows, K) > d->smem_optin - 256)
+    return fail(QZ_ERR_UNSUPPORTED, "qz_gemv_w4: K too large for the staged activations");
+  qz::GemvArgs a{reinterpret_cast<const int8_t*>(q4), scale, x, y, residual, N, K, ng};
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // Eight-row groups for tall matrices whose rows are whole 512-byte
+  // segments (the lm_head); two-row groups otherwise, including rows with a
+  // partial last segment.
+  const bool full = (K / 2) % qz::kW4Seg == 0;
+  const bool tall = full && qz::cdiv(N, int64_t(kW4TallRows) * qz::kWarps) >= d->sms;
+  if (tall)
+    return ng == 1 ? launch_gemv_w4<kW4TallRows, true, qz::KFULL>(*d, a, st)
+                   : launch_gemv_w4<kW4TallRows, false, qz::KFULL>(*d, a, st);
+  if (full)
+    return ng == 1 ? launch_gemv_w4<kW4Rows, true, qz::KFULL>(*d, a, st)
+                   : launch_gemv_w4<kW4Rows, false, qz::KFULL>(*d, a, st);
+  return ng == 1 ? launch_gemv_w4<kW4Rows, true, qz::KANY>(*d, a, st)
+                 : launch_gemv_w4<kW4Rows, false, qz::KANY>(*d, a, st);
 }
 
 int qz_gemm_w8(const int8_t* q, const float* scale, int64_t ng, const float* X, float* Y,

@@ -213,6 +213,31 @@ __device__ __forceinline__ void dot16_acc(const uint4& q, const f2_t* x, f2_t& a
   dot4_acc(q.w, x[6], x[7], acc);
 }
 
+// ---------------------------------------------------------------------------
+// int4 weights (two per byte, element 2i in the low nibble, two's complement,
+// symmetric in [-7, 7]). After the bias XOR a nibble holds n + 8 in 0..15.
+// Masked where it lies, at bit p(t) = 4t for t < 5 (nibbles 5..7 are shifted
+// right by 12 first: p = 8, 12, 16), it is the bit pattern of the subnormal
+// float (n + 8) * 2^(p - 149): no magic constant, no subtraction, one AND per
+// weight. The activations are staged as x * 2^(85 - p(t)) (|x| < 2^43 stays
+// finite), so each product is (n + 8) * x * 2^-64 in one FMA (fma.rn.f32x2
+// keeps subnormal inputs); the caller scales the sum by 2^64 and subtracts
+// 8 * sum(x) over the same weights. The packed FMA has no .ftz, so the
+// subnormal operands are exact.
+// ---------------------------------------------------------------------------
+__host__ __device__ constexpr int w4_pos(int t) { return t < 5 ? 4 * t : 4 * (t - 3); }
+
+// acc += sum_{t<8} x''[t] * f(nibble t of w); x01..x67 are the staged pairs.
+__device__ __forceinline__ void dot8_w4_acc(uint32_t w, f2_t x01, f2_t x23, f2_t x45, f2_t x67,
+                                            f2_t& acc) {
+  const uint32_t u = w ^ 0x88888888u;
+  const uint32_t v = u >> 12;
+  acc = f2_fma(x01, f2_pack(u & 0xFu, u & 0xF0u), acc);
+  acc = f2_fma(x23, f2_pack(u & 0xF00u, u & 0xF000u), acc);
+  acc = f2_fma(x45, f2_pack(u & 0xF0000u, v & 0xF00u), acc);
+  acc = f2_fma(x67, f2_pack(v & 0xF000u, v & 0xF0000u), acc);
+}
+
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {
   uint4 v;
   asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"

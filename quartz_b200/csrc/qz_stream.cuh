@@ -446,6 +446,171 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_kernel(const GemvArgs a) 
 }
 
 // ---------------------------------------------------------------------------
+// int4 GEMV (M = 1): rows of K / 2 bytes streamed through a per-warp
+// cp.async ring like the int8 kernel's, activations staged once per CTA in the
+// conflict-free layout of stage_x, pre-scaled for the subnormal widening of
+// dot8_w4_acc. K % 32 == 0, so a lane's 16-byte chunk (32 weights) never
+// straddles a scale group.
+// ---------------------------------------------------------------------------
+// Stage x * 2^(85 - p(j mod 8)) in the layout of stage_x, and the sum of
+// each 32-weight chunk's activations into csum[K / 32] (one thread per chunk,
+// in index order, so every CTA computes the same sums). Ends with a barrier.
+__device__ __forceinline__ void stage_x_w4(float* xs, float* csum, const float* x, int64_t K,
+                                           int tid, int nthr) {
+  const int64_t nch = K / 16;
+  for (int64_t i = tid; i < K; i += nthr) {
+    const int64_t c = i >> 4, j = i & 15;
+    const float s = __int_as_float((127 + 85 - w4_pos(static_cast<int>(i & 7))) << 23);
+    xs[((j >> 2) * nch + c) * 4 + (j & 3)] = x[i] * s;
+  }
+  for (int64_t c = tid; c < K / 32; c += nthr) {
+    float t = 0.f;
+#pragma unroll 8
+    for (int e = 0; e < 32; ++e) t += x[c * 32 + e];
+    csum[c] = t;
+  }
+  __syncthreads();
+}
+
+constexpr float kW4Unscale = 18446744073709551616.0f;   // 2^64
+
+// Rows of K / 2 bytes travel in segments of kW4Seg = 512 bytes (1024 weights),
+// R rows per item, so an item is 4 KB at R = 8 like the int8 kernel's 4 x 1 KB
+// and every lane copies and reads one 16-byte chunk of each row.
+constexpr int kW4Seg = 512;
+
+// Shared memory before the ring: the staged activations, then the chunk sums.
+__host__ __device__ inline int w4_x_bytes(int64_t K) {
+  return stream_x_bytes(K) + static_cast<int>(((K / 32) * 4 + 127) / 128 * 128);
+}
+
+template <int R, int KM, int D, class RowFn>
+__device__ __forceinline__ void issue_item_w4(const Walk<R, D>& w, uint32_t ring,
+                                              const Cursor<D>& c, int lane, RowFn rowfn) {
+  if (c.g < w.ngrp) {
+    const int64_t k0 = static_cast<int64_t>(c.seg) * kW4Seg;
+    const int64_t slen = KM == KANY ? min64(kW4Seg, w.K - k0) : kW4Seg;
+    const uint32_t slot = ring + static_cast<uint32_t>(c.slot * R * kW4Seg);
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int64_t row = rowfn(c.g, r);
+      if (row >= 0 && (KM != KANY || lane * 16 < slen))
+        cp_async16(slot + r * kW4Seg + lane * 16, w.q + row * w.K + k0 + lane * 16);
+    }
+  }
+  cp_async_commit();
+}
+
+template <int R, bool PER_ROW, int KM, int D, class ScaleFn>
+__device__ __forceinline__ void accumulate_item_w4(const Walk<R, D>& w, const uint8_t* ring,
+                                                   const uint8_t* xs, const float* csum,
+                                                   int64_t K, const Cursor<D>& c, int lane,
+                                                   int64_t G, float (&accs)[R],
+                                                   ScaleFn scale_of) {
+  const int64_t k0 = static_cast<int64_t>(c.seg) * kW4Seg;
+  const int64_t slen = KM == KANY ? min64(kW4Seg, w.K - k0) : kW4Seg;
+  if (KM == KANY && lane * 16 >= slen) return;
+  const uint8_t* slot = ring + c.slot * R * kW4Seg + lane * 16;
+  const int64_t nch = K / 16;
+  const int64_t gb = k0 / 16 + lane;            // 16-byte chunk = weights [32 gb, 32 gb + 32)
+  // both halves of the chunk's activations, then one row's chunk dot at a time
+  f2_t xa[8], xb[8];
+  load_x16(xs, nch, 2 * gb, xa);
+  load_x16(xs, nch, 2 * gb + 1, xb);
+  const int64_t grp = PER_ROW ? 0 : (gb * 32) / G;
+  const float off = PER_ROW ? 0.f : 8.f * csum[gb];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const uint4 qv = *reinterpret_cast<const uint4*>(slot + r * kW4Seg);
+    f2_t d = 0ull;
+    dot8_w4_acc(qv.x, xa[0], xa[1], xa[2], xa[3], d);
+    dot8_w4_acc(qv.y, xa[4], xa[5], xa[6], xa[7], d);
+    dot8_w4_acc(qv.z, xb[0], xb[1], xb[2], xb[3], d);
+    dot8_w4_acc(qv.w, xb[4], xb[5], xb[6], xb[7], d);
+    const float2 p = f2_unpack(d);
+    if (PER_ROW)
+      accs[r] += p.x + p.y;                     // scaled and corrected once per row
+    else
+      accs[r] = fmaf(fmaf(p.x + p.y, kW4Unscale, -off), scale_of(c.g, r, grp), accs[r]);
+  }
+}
+
+// y[n] = sum_g scale[n, g] sum_j q4[n, j] x[j] for q4 [N, K / 2] packed
+// bytes (a.q), K weights per row (a.K). KM is the mode of the row length in
+// bytes: KFULL when K / 2 is a multiple of kW4Seg, else KANY.
+template <int R, bool PER_ROW, int KM, int MINB>
+__global__ void __launch_bounds__(kThreads, MINB) gemv_w4_kernel(const GemvArgs a) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  float* xs = reinterpret_cast<float*>(smem);
+  float* csum = reinterpret_cast<float*>(smem + stream_x_bytes(a.K));
+  const uint8_t* ring = smem + w4_x_bytes(a.K) + warp * kDepth * R * kW4Seg;
+  const uint32_t ring_s = smem_u32(ring);
+  __shared__ float s_off;                       // 8 * sum(x), the per-row correction
+
+  const int64_t nw = static_cast<int64_t>(gridDim.x) * kWarps;
+  const int64_t wg = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
+  int64_t r0, r1;
+  split_range(a.N, nw, wg, r0, r1);
+  const int64_t kb = a.K / 2;                   // bytes per row
+  const Walk<R> w{a.q, kb, cdiv(r1 - r0, R), static_cast<int>(cdiv(kb, kW4Seg)), 0};
+  auto rowfn = [&](int64_t g, int r) -> int64_t {
+    const int64_t row = r0 + g * R + r;
+    return row < r1 ? row : -1;
+  };
+  issue_item_w4<R, KM>(w, ring_s, cursor_at(w, 0), lane, rowfn);
+  issue_item_w4<R, KM>(w, ring_s, cursor_at(w, kDepth - 1), lane, rowfn);
+  pdl_trigger();
+  pdl_wait();
+  stage_x_w4(xs, csum, a.x, a.K, tid, kThreads);
+  if (PER_ROW && warp == 0) {
+    float t = 0.f;
+    for (int64_t c = lane; c < a.K / 32; c += 32) t += csum[c];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    if (lane == 0) s_off = 8.f * t;
+  }
+  __syncthreads();
+
+  const int64_t G = a.K / a.ng;
+  auto scale_of = [&](int64_t g, int r, int64_t grp) -> float {
+    const int64_t row = r0 + g * R + r;
+    return row < r1 ? __ldg(a.scale + row * a.ng + grp) : 0.f;
+  };
+  float accs[R];
+  Cursor<kDepth> cur = cursor_at(w, 0);
+  Cursor<kDepth> ahead = cursor_at(w, kDepth - 1);
+  bool first = true;
+  for (; cur.g < w.ngrp; cur.next(w.nseg), ahead.next(w.nseg)) {
+    if (first)
+      first = false;                            // item D-1 went out before the wait
+    else if (ahead.g < w.ngrp)
+      issue_item_w4<R, KM>(w, ring_s, ahead, lane, rowfn);
+    else
+      cp_async_commit();
+    cp_async_wait<kDepth - 1>();
+    if (cur.seg == 0) {
+#pragma unroll
+      for (int r = 0; r < R; ++r) accs[r] = 0.f;
+    }
+    accumulate_item_w4<R, PER_ROW, KM>(w, ring, reinterpret_cast<const uint8_t*>(xs), csum, a.K,
+                                       cur, lane, G, accs, scale_of);
+    if (cur.seg == w.nseg - 1) {
+      const f2_t unused[R] = {};
+      const float sum = reduce_rows<R, false>(unused, accs, lane);
+      const int r = reduced_row<R>(lane);
+      const int64_t row = r0 + cur.g * R + r;
+      if (r >= 0 && row < r1) {
+        float o = PER_ROW ? fmaf(sum, kW4Unscale, -s_off) * __ldg(a.scale + row) : sum;
+        if (a.residual) o += a.residual[row];
+        a.y[row] = o;
+      }
+    }
+  }
+  cp_async_wait<0>();
+}
+
+// ---------------------------------------------------------------------------
 // Fused MLP (M = 1). Phase 1 walks "unit groups" of R/2 intermediate units,
 // stored as R/2 gate rows followed by the matching R/2 up rows; its epilogue
 // writes abuf[n] = silu(gate_n . x) * (up_n . x). A grid-wide barrier (bounded

@@ -185,6 +185,38 @@ def mlp_workspace(device) -> torch.Tensor:
     return ws
 
 
+def gemv_w4(q4, scale, x, y=None, residual=None):
+    """int4 weights: y[n] = sum_g scale[n,g] sum_{j<G} x[gG+j] q[n,gG+j]
+    (+ residual[n]), q4 uint8 [N, K/2] packed two weights per byte
+    (quartz_b200.quantize.pack_int4)."""
+    if not isinstance(q4, torch.Tensor) or q4.dtype != torch.uint8 or q4.dim() != 2:
+        raise TypeError("q4 must be a 2-D uint8 CUDA tensor")
+    if not q4.is_cuda or not q4.is_contiguous():
+        raise ValueError("q4 must be a contiguous CUDA tensor")
+    N, K = q4.shape[0], 2 * q4.shape[1]
+    _need(scale, torch.float32, "scale", 2)
+    if scale.shape[0] != N:
+        raise ValueError("scale and q4 disagree on the number of rows")
+    ng = scale.shape[1]
+    ensure_device(q4.device)
+    _need(x, torch.float32, "x")
+    if x.numel() != K:
+        raise ValueError(f"x has {x.numel()} elements, expected K={K}")
+    if y is None:
+        y = torch.empty(N, dtype=torch.float32, device=q4.device)
+    _need(y, torch.float32, "y")
+    if y.numel() != N:
+        raise ValueError(f"y has {y.numel()} elements, expected N={N}")
+    if residual is not None:
+        _need(residual, torch.float32, "residual")
+    _same_device(q4.device, scale, x, y, residual)
+    with torch.cuda.device(q4.device):
+        _lib.check(_lib.load().qz_gemv_w4(q4.data_ptr(), scale.data_ptr(), ng, x.data_ptr(),
+                                          y.data_ptr(), N, K, _ptr(residual),
+                                          _stream_ptr(q4.device)))
+    return y
+
+
 def fused_mlp(gu_q, gu_s, x, down_q, down_s, abuf=None, out=None, residual=None, norm_w=None,
               eps=1e-6):
     """out = down(silu(gate.x) * (up.x)) (+ residual) for one token (M = 1).

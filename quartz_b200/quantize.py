@@ -1,4 +1,4 @@
-"""Load-time symmetric int8 quantiser (host, numpy) and the dequantising row gather.
+"""Load-time symmetric int8 (and int4) quantisers (host, numpy) and the dequantising row gather.
 
 These produce the operands of the int8 weight-only path; they run once at model
 load, never on the decode hot path, so they stay numpy on the host.
@@ -43,6 +43,52 @@ def dequantize_symmetric(q: np.ndarray, scale: np.ndarray, group_size: int | Non
     G = K // ng
     qf = q.astype(np.float32).reshape(*shp[:-1], ng, G)
     return (qf * scale[..., None]).reshape(shp).astype(np.float32)
+
+
+def quantize_symmetric_int4(W: np.ndarray, group_size: int | None = None):
+    """(N, K) fp32 -> (q4 uint8 (N, K // 2) packed, scale fp32 (N, ng)).
+
+    The 4-bit twin of ``quantize_symmetric`` (quartz keeps 4-bit weights as
+    future work, quartz/config.py:98): scale = absmax / 7 per group (1.0 for
+    an all-zero group), q = clip(round_half_even(W / scale), -7, 7), packed
+    two per byte by ``pack_int4``. K must be even.
+    """
+    W = np.ascontiguousarray(W, dtype=np.float32)
+    N, K = W.shape
+    G = group_size or K
+    if K % G != 0:
+        raise ValueError(f"group_size {G} does not divide input dim {K}")
+    if K % 2:
+        raise ValueError("int4 packing needs an even input dim")
+    ng = K // G
+    Wg = W.reshape(N, ng, G)
+    scale = (np.abs(Wg).max(axis=2) / 7.0).astype(np.float32)
+    scale[scale == 0] = 1.0
+    q = np.clip(np.round(Wg / scale[:, :, None]), -7, 7).astype(np.int8).reshape(N, K)
+    return pack_int4(q), np.ascontiguousarray(scale)
+
+
+def pack_int4(q: np.ndarray) -> np.ndarray:
+    """int8 (..., K) in [-8, 7] -> uint8 (..., K // 2): element 2i in the low
+    nibble of byte i, element 2i + 1 in the high nibble, two's complement."""
+    q = np.asarray(q, dtype=np.int8)
+    if q.shape[-1] % 2:
+        raise ValueError("int4 packing needs an even last dim")
+    u = q.astype(np.uint8) & 0x0F
+    return np.ascontiguousarray(u[..., 0::2] | (u[..., 1::2] << 4))
+
+
+def unpack_int4(q4: np.ndarray) -> np.ndarray:
+    """uint8 (..., K // 2) -> int8 (..., K), the inverse of ``pack_int4``."""
+    q4 = np.asarray(q4, dtype=np.uint8)
+    lo = (q4 & 0x0F).astype(np.int8)
+    hi = (q4 >> 4).astype(np.int8)
+    lo = np.where(lo > 7, lo - 16, lo).astype(np.int8)
+    hi = np.where(hi > 7, hi - 16, hi).astype(np.int8)
+    out = np.empty(q4.shape[:-1] + (2 * q4.shape[-1],), np.int8)
+    out[..., 0::2] = lo
+    out[..., 1::2] = hi
+    return out
 
 
 def stack_gate_up(gate_q, gate_s, up_q, up_s):

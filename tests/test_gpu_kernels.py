@@ -211,3 +211,40 @@ def test_device_api_rejects_bad_args(K):
         device.gemv(q, torch.ones((4, 3), device="cuda"), torch.zeros(64, device="cuda"))
     with pytest.raises(TypeError):
         device.gemv(q.float(), torch.ones((4, 1), device="cuda"), torch.zeros(64, device="cuda"))
+
+
+@pytest.mark.parametrize("N,Kd,group_size,res", [(151936, 1024, None, False),
+                                                 (4096, 4096, 128, False),
+                                                 (1000, 1056, None, True),
+                                                 (3072, 2048, 32, False),
+                                                 (77, 64, None, False),
+                                                 (20000, 2048, 64, True)])
+def test_w4a32_gemv_vs_oracle(K, N, Kd, group_size, res):
+    """int4 weights (two per byte) through the numpy API and the torch API
+    against the numpy oracle: eight-row groups (lm_head shape; 20000 rows with
+    group scales and a residual), two-row groups with group scales, rows that
+    are not a whole number of 512-byte segments (K = 1056, K = 64)."""
+    from quartz_b200 import device
+    from quartz_b200.quantize import quantize_symmetric_int4
+    rng = np.random.default_rng(N + Kd)
+    W = (rng.standard_normal((N, Kd)) * 0.02).astype(np.float32)
+    q4, s = quantize_symmetric_int4(W, group_size)
+    x = rng.standard_normal(Kd).astype(np.float32)
+    r = rng.standard_normal(N).astype(np.float32) if res else None
+    ref = np.empty(N, np.float32)
+    oracle.w4a32_gemv(q4, s, x, ref)
+    if res:
+        ref = ref + r
+    if not res:
+        y = np.empty(N, np.float32)
+        K.w4a32_gemv(q4, s, x, y)
+        G.assert_close(y, ref, what=f"w4 numpy {N}x{Kd}")
+    yd = device.gemv_w4(_dev(q4), _dev(s), _dev(x), residual=_dev(r) if res else None)
+    G.assert_close(yd.cpu().numpy(), ref, what=f"w4 torch {N}x{Kd}")
+
+
+def test_w4a32_gemv_rejects_bad_shapes(K):
+    from quartz_b200 import device
+    q4 = torch.zeros(8, 24, dtype=torch.uint8, device="cuda")      # K = 48
+    with pytest.raises(Exception, match="multiples of 32"):
+        device.gemv_w4(q4, torch.ones(8, 1, device="cuda"), torch.ones(48, device="cuda"))
