@@ -100,6 +100,8 @@ def mlp_algorithmic_bytes(H, I, ng=1, ngd=1, M=1) -> int:
 #
 #   python -m quartz_b200.workloads gemm M N K      tensor-core GEMM, 3 calls
 #   python -m quartz_b200.workloads mlp             28-layer fused MLP body, once
+#   python -m quartz_b200.workloads lm4             lm_head GEMV, 3 int8 then 3 int4
+#                                                   calls on one N(0, 0.02) draw
 #   python -m quartz_b200.workloads decode [--persistent] [--tokens T]
 #                                                   Qwen3-0.6B, 512 prefilled KV
 #                                                   positions, T eager tokens
@@ -119,6 +121,7 @@ def _main(argv=None) -> None:
     g.add_argument("N", type=int)
     g.add_argument("K", type=int)
     sub.add_parser("mlp")
+    sub.add_parser("lm4")
     d = sub.add_parser("decode")
     d.add_argument("--persistent", action="store_true")
     d.add_argument("--tokens", type=int, default=3)
@@ -137,6 +140,20 @@ def _main(argv=None) -> None:
             Y = qd.gemm(q, s, X)
         torch.cuda.synchronize()
         print(f"gemm {a.M}x{a.N}x{a.K}: |Y|max {float(Y.abs().max()):.4g}")
+    elif a.what == "lm4":
+        from .quantize import quantize_symmetric, quantize_symmetric_int4
+        rng = np.random.default_rng(0)
+        W = rng.standard_normal((LM_HEAD_N, LM_HEAD_K), dtype=np.float32) * np.float32(0.02)
+        (q8, s8), (q4, s4) = quantize_symmetric(W), quantize_symmetric_int4(W)
+        x = torch.from_numpy(rng.standard_normal(LM_HEAD_K, dtype=np.float32)).to(dev)
+        t = lambda v: torch.from_numpy(v).to(dev)  # noqa: E731
+        q8d, s8d, q4d, s4d = t(q8), t(s8), t(q4), t(s4)
+        for _ in range(3):
+            y8 = qd.gemv(q8d, s8d, x)
+        for _ in range(3):
+            y4 = qd.gemv_w4(q4d, s4d, x)
+        torch.cuda.synchronize()
+        print(f"lm4: |y8|max {float(y8.abs().max()):.4g}, |y4|max {float(y4.abs().max()):.4g}")
     elif a.what == "mlp":
         for l in range(MLP_LAYERS):
             m = mlp_case(MLP_H, MLP_I, seed=MLP_LAYER_SEED0 + l)
