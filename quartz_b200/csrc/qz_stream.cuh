@@ -260,6 +260,21 @@ __device__ __forceinline__ float reduce_rows(const f2_t (&acc)[R], const float (
   }
   return warp_reduce8(v, lane);
 }
+// The same for R float partial sums, one per row.
+template <int R>
+__device__ __forceinline__ float reduce_row_sums(const float (&accs)[R], int lane) {
+  float v[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) v[r] = r < R ? accs[r] : 0.f;
+  if (R == 1) {
+    float s = v[0];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    return s;
+  }
+  return warp_reduce8(v, lane);
+}
+
 
 // The row (within its group) that this lane holds after reduce_rows, or -1.
 template <int R>
@@ -596,8 +611,7 @@ __global__ void __launch_bounds__(kThreads, MINB) gemv_w4_kernel(const GemvArgs 
     accumulate_item_w4<R, PER_ROW, KM>(w, ring, reinterpret_cast<const uint8_t*>(xs), csum, a.K,
                                        cur, lane, G, accs, scale_of);
     if (cur.seg == w.nseg - 1) {
-      const f2_t unused[R] = {};
-      const float sum = reduce_rows<R, false>(unused, accs, lane);
+      const float sum = reduce_row_sums<R>(accs, lane);
       const int r = reduced_row<R>(lane);
       const int64_t row = r0 + cur.g * R + r;
       if (r >= 0 && row < r1) {
