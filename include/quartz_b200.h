@@ -65,7 +65,9 @@ int qz_gemv_w8(const int8_t* q, const float* scale, int64_t ng, const float* x, 
  * copied into x_pin (pinned, K floats) and on to x_dev, the GEMV writes y_dev,
  * and y comes back through y_pin (pinned, N floats) into y_host in chunks, the
  * host copy of one chunk overlapping the transfer of the next. q and scale
- * are device pointers. Synchronises with the stream; allocates nothing.
+ * are device pointers. Synchronises with the stream. Allocates no memory;
+ * the first call on a thread and device creates the 16 events it reuses
+ * for the chunked copy.
  */
 int qz_gemv_w8_host(const int8_t* q, const float* scale, int64_t ng, const float* x_host,
                     float* y_host, int64_t N, int64_t K, float* x_pin, float* y_pin,

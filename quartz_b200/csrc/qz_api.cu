@@ -481,9 +481,18 @@ int copy_events(cudaEvent_t** out) {
   QZ_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices) return fail(QZ_ERR_UNSUPPORTED, "device index out of range");
   cudaEvent_t* ev = t_copy_ev[dev];
-  if (!ev[0])
-    for (int i = 0; i < kHostChunks; ++i)
-      QZ_CUDA(cudaEventCreateWithFlags(&ev[i], cudaEventDisableTiming));
+  if (!ev[kHostChunks - 1]) {
+    // all or nothing: a failed creation leaves the set empty for the next call
+    cudaEvent_t fresh[kHostChunks] = {};
+    for (int i = 0; i < kHostChunks; ++i) {
+      const cudaError_t e = cudaEventCreateWithFlags(&fresh[i], cudaEventDisableTiming);
+      if (e != cudaSuccess) {
+        for (int j = 0; j < i; ++j) (void)cudaEventDestroy(fresh[j]);
+        return fail(QZ_ERR_CUDA, std::string("cudaEventCreateWithFlags: ") + cudaGetErrorString(e));
+      }
+    }
+    for (int i = 0; i < kHostChunks; ++i) ev[i] = fresh[i];
+  }
   *out = ev;
   return QZ_OK;
 }
