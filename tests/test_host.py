@@ -34,6 +34,37 @@ def test_library_exports_every_declared_symbol():
     assert set(declared) <= exported
 
 
+def test_ctypes_signatures_match_the_header_prototypes():
+    """Every declared prototype and its ctypes binding agree argument by
+    argument: pointers with pointers, and each scalar with its C type."""
+    from quartz_b200 import _lib
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    protos = re.findall(r"^int\s+(qz_\w+)\s*\(([^)]*)\)\s*;", text, flags=re.M | re.S)
+    assert len(protos) == len(_declared())
+    scalar = {"int64_t": ctypes.c_int64, "int": ctypes.c_int, "size_t": ctypes.c_size_t,
+              "float": ctypes.c_float, "uint32_t": ctypes.c_uint32}
+
+    def kind(t):
+        if t in (ctypes.c_void_p, ctypes.c_char_p) or issubclass(t, ctypes._Pointer):
+            return "ptr"
+        return t
+
+    for name, params in protos:
+        want = []
+        for prm in (x.strip() for x in params.split(",")):
+            if not prm or prm == "void":
+                continue
+            if "*" in prm:
+                want.append("ptr")
+            else:
+                ctype = prm.rsplit(None, 1)[0].replace("const", "").strip()
+                assert ctype in scalar, f"{name}: unexpected parameter type {ctype!r}"
+                want.append(scalar[ctype])
+        got = [kind(t) for t in _lib.SIGNATURES[name][0]]
+        assert got == want, f"{name}: ctypes {got} vs header {want}"
+        assert _lib.SIGNATURES[name][1] is ctypes.c_int, f"{name}: status return"
+
+
 def test_version_and_error_buffer():
     from quartz_b200 import _lib
     lib = _lib.load()

@@ -54,3 +54,26 @@ def test_int4_oracle_matches_dequantised_matmul(ng):
     q = unpack_int4(q4).astype(np.float64).reshape(N, ng, K // ng)
     ref = ((q * s.astype(np.float64)[:, :, None]).reshape(N, K) @ x.astype(np.float64))
     np.testing.assert_allclose(y, ref.astype(np.float32), rtol=1e-6, atol=1e-6)
+
+
+def test_w4a32_gemv_validates_before_touching_the_gpu():
+    """The numpy entry point rejects bad operands on the host (no GPU needed)."""
+    from quartz_b200.kernels import w4a32_gemv
+    q4 = np.zeros((4, 32), np.uint8)          # K = 64
+    s = np.ones((4, 1), np.float32)
+    x = np.zeros(64, np.float32)
+    y = np.zeros(4, np.float32)
+    with pytest.raises(TypeError, match="uint8"):
+        w4a32_gemv(q4.view(np.int8), s, x, y)
+    with pytest.raises(ValueError, match="rows"):
+        w4a32_gemv(q4, np.ones((3, 1), np.float32), x, y)
+    with pytest.raises(ValueError, match="do not tile"):
+        w4a32_gemv(q4, np.ones((4, 3), np.float32), x, y)
+    with pytest.raises(ValueError, match="shape"):
+        w4a32_gemv(q4, s, np.zeros(32, np.float32), y)
+    with pytest.raises(TypeError, match="y must be"):
+        w4a32_gemv(q4, s, x, np.zeros(4, np.float64))
+    with pytest.raises(ValueError, match="writeable"):
+        ro = np.zeros(4, np.float32)
+        ro.setflags(write=False)
+        w4a32_gemv(q4, s, x, ro)
