@@ -81,7 +81,8 @@ int qz_gemv_w8_host(const int8_t* q, const float* scale, int64_t ng, const float
  * in the reference: quartz keeps a `bits` field for 4-bit weights as future
  * work (quartz/config.py:98). K and the group size G = K / ng must be
  * multiples of 32 and q4 16-byte aligned; other shapes return
- * QZ_ERR_INVALID. residual may be NULL.
+ * QZ_ERR_INVALID. residual may be NULL. The kernel stages x scaled by up to
+ * 2^85, so it is exact for |x| < 2^43 (activations beyond that overflow).
  */
 int qz_gemv_w4(const uint8_t* q4, const float* scale, int64_t ng, const float* x, float* y,
                int64_t N, int64_t K, const float* residual, void* stream);

@@ -19,7 +19,8 @@ from .. import device as _dev
 
 def w4a32_gemv(q4, scale, x, y) -> None:
     """Decode GEMV (M=1) on int4 weights. q4:(N,K/2) uint8 packed; scale:(N,ng)
-    f32; x:(K,) f32; y:(N,) f32 out. y[n] = sum_g scale[n,g] * sum_j x[gG+j] q[n,gG+j]."""
+    f32; x:(K,) f32; y:(N,) f32 out. y[n] = sum_g scale[n,g] * sum_j x[gG+j] q[n,gG+j].
+    K and K // ng must be multiples of 32; exact for |x| < 2^43."""
     if any(isinstance(t, torch.Tensor) for t in (q4, scale, x, y)):
         _dev.gemv_w4(q4, scale, x.reshape(-1), y)
         return
