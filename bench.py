@@ -43,6 +43,16 @@ UNIT = "GB/s"
 WORKLOAD = "qwen3-0.6b lm_head int8 GEMV [151936x1024], M=1, per-row scale"
 
 
+def bench_config(world: int, copies: int) -> dict:
+    """The workload description both arms print (identical by construction)."""
+    return {"workload": WORKLOAD, "seed": 0, "weight_copies": copies,
+            "l2": f"inputs larger than L2: {copies} rotating weight copies of "
+                  f"{LM_HEAD_N * LM_HEAD_K / 1e6:.1f} MB",
+            "bytes_per_step_per_gpu": gemv_algorithmic_bytes(LM_HEAD_N, LM_HEAD_K),
+            "parallelism": "replicas (one lm_head GEMV stream per GPU)" if world > 1
+            else "single GPU"}
+
+
 def _peaks():
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
@@ -172,7 +182,7 @@ def run_reference(args) -> dict:
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(dt * 1e3, 4), "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "int8 weights, fp32 accumulate", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "seed": 0},
+        "config": bench_config(args.gpus, args.copies),
         "cpu_baseline": {"value": round(gbs, 3), "unit": UNIT, "cores": oracle.threads(),
                          "kind": "port",
                          "sample": f"full lm_head GEMV per step, {args.steps} steps "
@@ -477,14 +487,58 @@ def _barrier(world: int) -> None:
     torch.cuda.synchronize()
 
 
-def run_tp(args, rank: int, world: int, dev) -> dict:
+def tp_layers_parity(rank: int, world: int, dev, case) -> dict:
+    """The sharded MLP and lm_head at this rank count against the oracle
+    before the tensor-parallel step is timed: the Qwen3-0.6B MLP layer (H 1024,
+    I 3072, seed 1000) at M = 1 (fused kernel, quartz/kernels/fused.py:27-65)
+    and M = 16 (per-op path, quartz/quantize.py:112-114), max |err| <= 1e-4 *
+    ||y||_inf; the lm_head workload's greedy token at M = 1 and 16 rows, equal
+    to the oracle's argmax unless the oracle's top two logits are closer than
+    that tolerance. Every rank checks, then the verdict is all-reduced."""
+    import torch
+    import oracle
+    from quartz_b200.sharding import ShardedLMHead, ShardedMLP
+    m = mlp_case(MLP_H, MLP_I, M=16, seed=MLP_LAYER_SEED0)
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a))  # noqa: E731
+    I = MLP_I
+    mlp = ShardedMLP(t(m.gu_q[:I]), t(m.gu_s[:I]), t(m.gu_q[I:]), t(m.gu_s[I:]), t(m.down_q),
+                     t(m.down_s), device=dev)
+    errs = {}
+    ref1 = np.empty(MLP_H, np.float32)
+    oracle.fused_mlp_decode(m.gu_q, m.gu_s, m.x[0], m.down_q, m.down_s,
+                            np.empty(I, np.float32), ref1)
+    got1 = mlp(t(m.x[:1]).to(dev)).cpu().numpy()[0]
+    errs["mlp_M1"] = float(np.abs(got1 - ref1).max() / np.abs(ref1).max())
+    ref16 = oracle.mlp_per_op(m.gu_q, m.gu_s, m.down_q, m.down_s, m.x)
+    got16 = mlp(t(m.x).to(dev)).cpu().numpy()
+    errs["mlp_M16"] = float(np.abs(got16 - ref16).max() / np.abs(ref16).max())
+    head = ShardedLMHead(t(case.q), t(case.scale), device=dev)
+    X = np.concatenate([case.x, np.random.default_rng(5).standard_normal(
+        (15, case.q.shape[1]), dtype=np.float32)])
+    Y = np.empty((16, case.q.shape[0]), np.float32)
+    oracle.w8a32_gemm(case.q, case.scale, X, Y)
+    toks = head.argmax(t(X).to(dev)).cpu().numpy()
+    tol = 1e-4 * np.abs(Y).max(axis=1)
+    near = Y[np.arange(16), toks] >= Y.max(axis=1) - tol
+    ok = max(errs.values()) <= 1e-4 and bool(near.all())
+    del mlp, head
+    torch.cuda.empty_cache()
+    if not _all_ranks_ok(ok, world):
+        raise SystemExit(f"sharded MLP / lm_head parity failed on {world} ranks (rank {rank}): "
+                         f"{errs}, argmax within tolerance {near.tolist()}")
+    return {"ranks": world, "rel_err": {k: float(f"{v:.3e}") for k, v in errs.items()},
+            "argmax_rows_equal": int((toks == Y.argmax(axis=1)).sum()), "argmax_rows": 16,
+            "match_oracle": True}
+
+
+def run_tp(args, rank: int, world: int, dev, case) -> dict:
     """Tensor-parallel Qwen3-8B shapes (hidden 4096, MLP 12288, vocab 151936,
     36 layers): per step, the 36 MLP layers (gate/up column-parallel, down
     row-parallel, all-reduce of the partials) and the vocab-parallel lm_head
     with the greedy (max, index) all-gather. Strong scaling: the whole model's
     int8 weights are split over the ranks. Weights are drawn on the device
     (int8 uniform, fp32 scales): timing does not depend on their values;
-    parity of this path is covered by the tests."""
+    the sharded layers are checked against the oracle first (tp_layers_parity)."""
     import torch
     from quartz_b200.sharding import ShardedLMHead, ShardedMLP, shard_range
     H, I, V, L = 4096, 12288, 151936, 36
@@ -497,6 +551,7 @@ def run_tp(args, rank: int, world: int, dev) -> dict:
     def s_(n):
         return torch.rand((n, 1), device=dev, generator=gen) * 2e-4 + 1e-4
 
+    parity = tp_layers_parity(rank, world, dev, case)
     lo, hi = shard_range(V, world, rank)
     head = ShardedLMHead.from_local(q_((hi - lo, H)), s_(hi - lo), V)
     ulo, uhi = shard_range(I, world, rank)
@@ -504,7 +559,8 @@ def run_tp(args, rank: int, world: int, dev) -> dict:
                                     q_((H, uhi - ulo)), s_(H), I) for _ in range(L)]
     weight_bytes = V * H + L * 3 * I * H
     out = {"workload": "qwen3-8b shapes: 36 TP MLP layers + vocab-parallel lm_head argmax",
-           "n_gpus": world, "scaling": "strong", "weight_bytes": weight_bytes}
+           "n_gpus": world, "scaling": "strong", "weight_bytes": weight_bytes,
+           "layers_parity": parity}
     for M in (1, 16):
         x = torch.randn((M, H), device=dev, generator=gen)
 
@@ -552,20 +608,67 @@ def run_tp(args, rank: int, world: int, dev) -> dict:
 TP_CTX, TP_TOKENS, TP_UNROLL = 2048, 64, 16
 
 
+def _all_ranks_ok(ok: bool, world: int) -> bool:
+    """True when every rank passed (one all-reduce, taken by every rank)."""
+    if world == 1:
+        return ok
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([1 if ok else 0], dtype=torch.int32,
+                     device=torch.device("cuda", torch.cuda.current_device()))
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return bool(t.item())
+
+
+def tp_parity_gate(rank: int, world: int, dev, allreduce: str) -> dict:
+    """Greedy tokens of the N-rank TPDecodeEngine against the reference's own
+    tokens before anything is timed: the Qwen3-0.6B architecture (16 query / 8
+    kv heads, MLP 3072 -- every split up to 8 ranks is whole), the seeded
+    synthetic checkpoint, 512 prefilled KV positions, 128 greedy tokens from
+    token 42, replayed from CUDA graphs of 16 tokens. Any rank's mismatch
+    stops every rank (SystemExit) after a common all-reduce of the verdict."""
+    import torch
+    from quartz_b200.model import QWEN3_0P6B, cached_int8_weights, norm_weights, seeded_kv
+    from quartz_b200.tp_decode import TPDecodeEngine
+    spec = QWEN3_0P6B
+    with np.load(REPO / "tests" / "golden" / "golden_model.npz") as z:
+        gold = z["qwen3_0p6b_kv512__tokens"].tolist()
+    eng = TPDecodeEngine(spec, cached_int8_weights(spec), norm_weights(spec),
+                         max_ctx=DECODE_KV + DECODE_TOKENS, max_prefill=1, device=dev,
+                         allreduce=allreduce)
+    eng.load_kv(seeded_kv(spec, DECODE_KV))
+    toks = eng.generate(DECODE_FIRST, DECODE_TOKENS, graph=True, unroll=DECODE_UNROLL)
+    eng.close()
+    del eng
+    torch.cuda.empty_cache()
+    ok = toks == gold
+    if not _all_ranks_ok(ok, world):
+        bad = next((i for i, (x, y) in enumerate(zip(toks, gold)) if x != y), None)
+        raise SystemExit(f"tensor-parallel decode parity failed ({allreduce}, {world} ranks, "
+                         f"rank {rank}): first differing token {bad}")
+    return {"case": "qwen3-0.6b architecture, 512 prefilled KV positions, 128 greedy tokens "
+                    "from token 42 (the reference's tokens)", "allreduce": allreduce,
+            "ranks": world, "tokens_match_reference": True}
+
+
 def run_tp_decode(args, rank: int, world: int, dev) -> dict:
     """Greedy decode of one Qwen3-8B sequence split over the ranks
     (TPDecodeEngine: head-sharded attention, unit-sharded MLP, vocab-sharded
     lm_head, two all-reduces per layer), at context 2048..2112, 64 tokens per
     pass replayed from CUDA graphs of 16. Weights are drawn on the device per
-    shard (timing does not depend on the values; the engine's tokens are
-    tested against the reference on smaller checkpoints)."""
+    shard (timing does not depend on the values). Before each all-reduce form
+    is timed, the same engine at the same rank count must reproduce the
+    reference's greedy tokens on the Qwen3-0.6B workload (tp_parity_gate)."""
     import torch
     from quartz_b200.model import QWEN3_8B, norm_weights
     from quartz_b200.tp_decode import TPDecodeEngine, random_tp_shard
     spec = QWEN3_8B
     stream = torch.cuda.current_stream()
 
+    gates = []
+
     def measure(allreduce: str) -> float:
+        gates.append(tp_parity_gate(rank, world, dev, allreduce))
         shard = random_tp_shard(spec, rank, world, dev)
         eng = TPDecodeEngine(spec, None, norm_weights(spec), max_ctx=TP_CTX + TP_TOKENS,
                              max_prefill=1, device=dev, presharded=shard, allreduce=allreduce)
@@ -621,7 +724,9 @@ def run_tp_decode(args, rank: int, world: int, dev) -> dict:
                                            "value": round(1.0 / (ms_peer * 1e-3), 1)},
             "with_nccl_allreduce": {"us_per_token": round(ms_nccl * 1e3, 1),
                                     "value": round(1.0 / (ms_nccl * 1e-3), 1)},
-            "allreduce_us_per_call": ar_us}
+            "allreduce_us_per_call": ar_us,
+            "tokens_match_reference": all(g["tokens_match_reference"] for g in gates),
+            "parity_gates": gates}
 
 
 def allreduce_latency(world: int, dev, n: int) -> dict:
@@ -696,39 +801,68 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
 
     stream = torch.cuda.current_stream()
     use_graph = not args.no_graph
+    graphs = []          # (graph, steps it holds); the timed region replays each once per pass
     if use_graph:
-        # One graph holds `chunk` consecutive steps; replays are enqueued back to back.
-        chunk = min(args.steps, 256)
-        g = torch.cuda.CUDAGraph()
+        # The K timed steps are whole graph replays: `chunk` steps per graph,
+        # the largest divisor of K up to 256, plus one graph for a remainder
+        # when K has no divisor of useful size.
+        chunk = max(d for d in range(1, min(args.steps, 256) + 1) if args.steps % d == 0)
+        if chunk < 32:
+            chunk = min(args.steps, 256)
+        full, rem = divmod(args.steps, chunk)
         s = torch.cuda.Stream()
         s.wait_stream(stream)
         with torch.cuda.stream(s):
             step(0)
         stream.wait_stream(s)
         torch.cuda.synchronize()
-        with torch.cuda.graph(g):
-            for i in range(chunk):
-                step(i)
+        def copy_of(i, n):
+            # weight copy of step i of an n-step graph: round robin, except that
+            # a graph never ends on copy 0, which the next replay starts with
+            if i == n - 1 and n > 1 and i % copies == 0:
+                return 1
+            return i % copies
+
+        for n in ([chunk] * (1 if full else 0)) + ([rem] if rem else []):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for i in range(n):
+                    step(copy_of(i, n))
+            graphs.append((g, n))
         torch.cuda.synchronize()
 
     def run(n):
+        """n steps exactly as the timed region runs them."""
         if use_graph:
-            full, rem = divmod(n, chunk)
-            for _ in range(full):
-                g.replay()
-            for i in range(rem):
-                step(i)
+            main_reps, tail = divmod(n, chunk)
+            for _ in range(main_reps):
+                graphs[0][0].replay()
+            if tail:
+                graphs[-1][0].replay()
         else:
             for i in range(n):
                 step(i)
 
-    run(args.warmup)
+    # Warm-up runs the timed path itself: every graph the timed region replays
+    # is replayed (and so uploaded) at least once, W steps or more in all.
+    if use_graph:
+        warm_done = 0
+        while warm_done < args.warmup:
+            run(args.steps)
+            warm_done += args.steps
+    else:
+        run(args.warmup)
+        warm_done = args.warmup
+    torch.cuda.synchronize()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
     clk = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
     if clk:
         clk.__enter__()
     _barrier(world)
+    # a short device-side delay ahead of the start event lets the host enqueue
+    # the timed launches before the GPU reaches them (no host gaps are timed)
+    torch.cuda._sleep(200_000)
     start.record(stream)
     run(args.steps)
     end.record(stream)
@@ -781,10 +915,9 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     _log(rank, "int4 GEMV done")
     dec = None if args.no_decode else run_decode(args, dev, world=world)
     _log(rank, "decode done")
-    tp = None if args.no_tp else run_tp(args, rank, world, dev)
+    tp = None if args.no_tp else run_tp(args, rank, world, dev, case)
     _log(rank, "tensor-parallel block done")
-    if use_graph:
-        del g
+    del graphs
 
     if rank != 0:
         return None
@@ -798,12 +931,10 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 5),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int8 weights, fp32 accumulate", "data": "synthetic",
-        "config": {"workload": WORKLOAD, "seed": 0, "weight_copies": copies,
-                   "l2": f"inputs larger than L2: {copies} rotating weight copies of "
-                         f"{N * K / 1e6:.1f} MB", "graph": use_graph,
-                   "bytes_per_step_per_gpu": nbytes,
-                   "parallelism": "replicas (one lm_head GEMV stream per GPU)" if world > 1
-                   else "single GPU"},
+        "config": bench_config(world, copies),
+        "timing": {"graph": use_graph, "graph_steps": chunk if use_graph else None,
+                   "warmup_steps_run": warm_done,
+                   "note": "warm-up replays the same CUDA graph(s) the timed region replays"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": UNIT,
                      "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                      "traffic": traffic, "per": "one GPU"},

@@ -155,9 +155,11 @@ int qz_mlp_workspace_bytes(void);
  *     cudaGetSymbolAddress (with that device current). Make that first call
  *     before any stream capture.
  *   - All calls share the one array, which keeps the last call's intermediate.
- *     The barrier count is cleared (cudaMemsetAsync on `stream`) at the start
- *     of every call. Calls that overlap on the GPU (different streams, or
- *     concurrent host threads) race on the array: serialise them.
+ *     The barrier count is cleared (cudaMemsetAsync on `stream`) after the
+ *     arguments are checked and before the one-launch kernel that uses it;
+ *     a refused call queues nothing. Calls that overlap on the GPU
+ *     (different streams, or concurrent host threads) race on the array:
+ *     serialise them.
  * Arguments and results are those of qz_fused_mlp_decode minus abuf/sync_ws.
  */
 int qz_fused_mlp_decode_noalloc(const int8_t* gu_q, const float* gu_s, int64_t ng, const float* x,

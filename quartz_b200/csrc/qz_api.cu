@@ -42,7 +42,7 @@ constexpr int kTallRows = 4;
 constexpr int kMinBlocks = 3;   // launch bound: CTAs per SM the register budget allows
 
 struct DeviceInfo {
-  bool ready = false;
+  std::atomic<bool> ready{false};   // set (release) once the fields below are final
   int sms = 0;
   int smem_optin = 0;   // max dynamic shared memory per block (opt-in)
   int coop = 0;         // cooperative launch supported
@@ -104,9 +104,9 @@ int device_info(DeviceInfo** out) {
   QZ_CUDA(cudaGetDevice(&dev));
   if (dev < 0 || dev >= kMaxDevices) return fail(QZ_ERR_UNSUPPORTED, "device index out of range");
   DeviceInfo& d = g_dev[dev];
-  if (!d.ready) {
+  if (!d.ready.load(std::memory_order_acquire)) {
     std::lock_guard<std::mutex> lock(g_dev_mu);
-    if (!d.ready) {
+    if (!d.ready.load(std::memory_order_relaxed)) {
       cudaDeviceProp p;
       QZ_CUDA(cudaGetDeviceProperties(&p, dev));
       if (p.major != 10)
@@ -124,7 +124,7 @@ int device_info(DeviceInfo** out) {
       QZ_CUDA((allow_gemv_w4_variants<2, true>(smem)));
       QZ_CUDA(allow_mlp_variants<kTallRows>(smem));
       QZ_CUDA(allow_mlp_variants<2>(smem));
-      d.ready = true;
+      d.ready.store(true, std::memory_order_release);
     }
   }
   *out = &d;
@@ -614,7 +614,8 @@ namespace {
 int mlp_impl(const int8_t* gu_q, const float* gu_s, int64_t ng, const float* x,
              const int8_t* down_q, const float* down_s, int64_t ngd, float* abuf, float* out,
              const float* residual, int64_t H, int64_t I, uint32_t* sync_ws, void* stream,
-             const qz::comm::PeerOut* po, const float* norm_w = nullptr, float eps = 0.f) {
+             const qz::comm::PeerOut* po, const float* norm_w = nullptr, float eps = 0.f,
+             bool clear_barrier = false) {
   if (int rc = check_weights(gu_q, gu_s, ng, 2 * I, H, "qz_fused_mlp_decode (gate|up)")) return rc;
   if (int rc = check_weights(down_q, down_s, ngd, H, I, "qz_fused_mlp_decode (down)")) return rc;
   if (H == 0) return QZ_OK;
@@ -640,6 +641,9 @@ int mlp_impl(const int8_t* gu_q, const float* gu_s, int64_t ng, const float* x,
     }
     return launch_generic_gemm(*d, down_q, down_s, ngd, abuf, out, residual, 1, H, I, st);
   }
+  // clear_barrier: the arrival count is zeroed (stream-ordered) right before
+  // the cooperative launch, the only path that uses it
+  if (clear_barrier) QZ_CUDA(cudaMemsetAsync(sync_ws, 0, sizeof(uint32_t), st));
   qz::MlpArgs a{gu_q, gu_s, x, down_q, down_s, abuf, out, residual, sync_ws, H, I, ng, ngd};
   if (po) a.po = *po;
   a.norm_w = norm_w;
@@ -801,11 +805,13 @@ int qz_fused_mlp_decode_noalloc(const int8_t* gu_q, const float* gu_s, int64_t n
   float* scratch = nullptr;
   if (int rc = noalloc_scratch(&scratch)) return rc;
   uint32_t* barrier = reinterpret_cast<uint32_t*>(scratch + kNoAllocMaxI);
-  // The barrier's arrival count must be zero when a call starts; a call whose
-  // wait gave up could have left it otherwise, so clear it (stream-ordered).
-  QZ_CUDA(cudaMemsetAsync(barrier, 0, sizeof(uint32_t), static_cast<cudaStream_t>(stream)));
-  return qz_fused_mlp_decode(gu_q, gu_s, ng, x, down_q, down_s, ngd, scratch, out, residual, H, I,
-                             barrier, stream);
+  // The barrier's arrival count must be zero when the cooperative kernel
+  // starts; a call whose wait gave up could have left it otherwise. mlp_impl
+  // checks the arguments first and clears it (stream-ordered) only on the
+  // path that launches that kernel, so a refused call or the two-launch
+  // fallback leaves nothing on the stream beyond its own kernels.
+  return mlp_impl(gu_q, gu_s, ng, x, down_q, down_s, ngd, scratch, out, residual, H, I, barrier,
+                  stream, nullptr, nullptr, 0.f, /*clear_barrier=*/true);
 }
 
 

@@ -158,6 +158,58 @@ def random_int8_weights(spec: ModelSpec, seed: int = 1234, std: float = 0.02,
         yield name, q, s
 
 
+def cached_int8_weights(spec: ModelSpec, seed: int = 1234, std: float = 0.02,
+                        cache_dir: str | None = None) -> list[tuple[str, np.ndarray, np.ndarray]]:
+    """random_int8_weights(spec, seed, std) as a list, kept in a per-host cache
+    file so that processes after the first (other ranks, later runs) load the
+    int8 tensors instead of drawing them again (the fp32 draws dominate: about
+    25 s for the Qwen3-0.6B checkpoint on one core). The first process to take
+    the file lock draws and writes the file; the others wait for it and load
+    it. Directory: `cache_dir`, else $QZ_CACHE_DIR, else the system temp dir."""
+    import fcntl
+    import hashlib
+    import os
+    import tempfile
+
+    key = hashlib.sha256(repr((spec, seed, std)).encode()).hexdigest()[:20]
+    root = cache_dir or os.environ.get("QZ_CACHE_DIR") or tempfile.gettempdir()
+    os.makedirs(root, exist_ok=True)
+    base = os.path.join(root, f"qz_int8_ckpt_{key}")
+    shapes = leaf_names(spec)
+
+    def load():
+        # two flat files (all q bytes, all scales) mapped read-only; the
+        # tensors are views into them, in leaf order
+        qb = np.load(base + "_q.npy", mmap_mode="r")
+        sb = np.load(base + "_s.npy", mmap_mode="r")
+        out, oq, os_ = [], 0, 0
+        for name, (n, k) in shapes:
+            if oq + n * k > qb.size or os_ + n > sb.size:
+                raise ValueError("cache file shorter than the checkpoint")
+            out.append((name, qb[oq:oq + n * k].reshape(n, k), sb[os_:os_ + n].reshape(n, 1)))
+            oq += n * k
+            os_ += n
+        return out
+
+    with open(base + ".lock", "w") as lk:
+        fcntl.flock(lk, fcntl.LOCK_EX)
+        try:
+            if os.path.exists(base + "_s.npy"):
+                try:
+                    return load()
+                except (OSError, ValueError):
+                    pass                     # damaged or partial: draw again
+            out = list(random_int8_weights(spec, seed, std))
+            for suffix, parts in (("_q", [q.reshape(-1) for _, q, _ in out]),
+                                  ("_s", [s_.reshape(-1) for _, _, s_ in out])):
+                tmp = f"{base}{suffix}.{os.getpid()}.tmp.npy"
+                np.save(tmp, np.concatenate(parts))
+                os.replace(tmp, base + suffix + ".npy")   # the scales file last: it marks completion
+            return out
+        finally:
+            fcntl.flock(lk, fcntl.LOCK_UN)
+
+
 def norm_weights(spec: ModelSpec) -> dict[str, np.ndarray]:
     """The RMSNorm weights of the synthetic checkpoints: all ones."""
     H, hd = spec.hidden, spec.head_dim

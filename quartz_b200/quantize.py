@@ -27,6 +27,24 @@ def quantize_symmetric(W: np.ndarray, group_size: int | None = None):
     G = group_size or K
     if K % G != 0:
         raise ValueError(f"group_size {G} does not divide input dim {K}")
+    if W.size >= _PARALLEL_ELEMS and N >= 2 * _THREADS:
+        # rows are independent: quantise row blocks on host threads (numpy
+        # releases the GIL in these loops); the bytes are those of one pass
+        from concurrent.futures import ThreadPoolExecutor
+        b = [N * i // _THREADS for i in range(_THREADS + 1)]
+        with ThreadPoolExecutor(_THREADS) as ex:
+            parts = list(ex.map(lambda i: _quantize_rows(W[b[i]:b[i + 1]], G), range(_THREADS)))
+        return (np.ascontiguousarray(np.concatenate([p[0] for p in parts])),
+                np.ascontiguousarray(np.concatenate([p[1] for p in parts])))
+    return _quantize_rows(W, G)
+
+
+_PARALLEL_ELEMS = 1 << 24
+_THREADS = 8
+
+
+def _quantize_rows(W: np.ndarray, G: int):
+    N, K = W.shape
     ng = K // G
     Wg = W.reshape(N, ng, G)
     scale = (np.abs(Wg).max(axis=2) / 127.0).astype(np.float32)

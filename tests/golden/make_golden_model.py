@@ -175,5 +175,7 @@ def main(ref_root: str, only=None):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference",
-         only=sys.argv[2].split(",") if len(sys.argv) > 2 else None)
+    if len(sys.argv) < 2:
+        raise SystemExit("usage: make_golden_model.py <path of the quartz source tree> "
+                         "[case,case,...]")
+    main(sys.argv[1], only=sys.argv[2].split(",") if len(sys.argv) > 2 else None)

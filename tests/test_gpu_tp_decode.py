@@ -1,8 +1,9 @@
 """Tensor-parallel decode (head-sharded attention, unit-sharded MLP, vocab-sharded
-lm_head, NCCL all-reduces) on 2+ GPUs: the greedy tokens must equal quartz's
-own on the same synthetic checkpoints (tests/golden/golden_model.npz), eager
-and CUDA-graph replay, prefill and prefilled-cache starts. Skipped on a
-single-GPU host. NVLS is left off (NCCL_NVLS_ENABLE=0)."""
+lm_head, NCCL / peer-memory / in-kernel all-reduces) on 2, 4 and 8 GPUs: the
+greedy tokens must equal quartz's own on the same synthetic checkpoints
+(tests/golden/golden_model.npz), eager and CUDA-graph replay, prefill and
+prefilled-cache starts. A rank count needs that many visible GPUs and is
+skipped otherwise. NVLS is left off (NCCL_NVLS_ENABLE=0)."""
 
 import datetime
 import json
@@ -26,7 +27,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, cids):
+def _worker(rank, world, port, cids, variants):
     import sys
     sys.path.insert(0, REPO)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -35,7 +36,7 @@ def _worker(rank, world, port, cids):
         "nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
         timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
     from quartz_b200 import device
-    from quartz_b200.model import ModelSpec, norm_weights, random_int8_weights, seeded_kv
+    from quartz_b200.model import ModelSpec, cached_int8_weights, norm_weights, seeded_kv
     from quartz_b200.tp_decode import TPDecodeEngine
     cases = {c["id"]: c for c in json.loads((GOLD / "cases_model.json").read_text())["cases"]}
     try:
@@ -45,10 +46,11 @@ def _worker(rank, world, port, cids):
             case = cases[cid]
             spec = ModelSpec.from_hf(case["cfg"], case["arch"])
             start = case.get("kv_len") or len(case["prompt"])
-            for allreduce, graph in (("nccl", False), ("nccl", True), ("peer", False),
-                                     ("peer", True), ("fused", False), ("fused", True)):
-                if graph is False:
-                    eng = TPDecodeEngine(spec, random_int8_weights(spec), norm_weights(spec),
+            eng_kind = None
+            for allreduce, graph in variants:
+                if graph is False or allreduce != eng_kind:
+                    eng_kind = allreduce
+                    eng = TPDecodeEngine(spec, cached_int8_weights(spec), norm_weights(spec),
                                          max_ctx=start + case["steps"],
                                          max_prefill=max(2, len(case.get("prompt", [])) or 2),
                                          device=torch.device("cuda", rank), allreduce=allreduce)
@@ -69,14 +71,27 @@ def _worker(rank, world, port, cids):
         torch.distributed.destroy_process_group()
 
 
-@pytest.mark.skipif(not torch.cuda.is_available() or torch.cuda.device_count() < 2,
-                    reason="needs 2 GPUs")
-def test_tp_decode_tokens_match_reference():
+ALL_VARIANTS = (("nccl", False), ("nccl", True), ("peer", False), ("peer", True),
+                ("fused", False), ("fused", True))
+# Cases whose head and unit counts divide by the rank count: the small models
+# have 2 kv heads; the Qwen3-0.6B (8 kv heads, MLP 3072) and Llama-3.2-1B (8 kv
+# heads, MLP 8192) architectures split up to 8 ways.
+TP_CASES = {
+    2: (["qwen3_small_kv", "llama_small_prompt", "qwen3_0p6b_kv512"], ALL_VARIANTS),
+    4: (["qwen3_0p6b_kv512"], ALL_VARIANTS),
+    8: (["qwen3_0p6b_kv512", "llama_1b_prompt512"], (("nccl", True), ("fused", False),
+                                                    ("fused", True))),
+}
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_decode_tokens_match_reference(world):
     """NCCL, peer-memory and in-kernel (fused) all-reduces, eager and graph replay."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
-    mp.spawn(_worker, args=(2, _free_port(),
-                            ["qwen3_small_kv", "llama_small_prompt", "qwen3_0p6b_kv512"]),
-             nprocs=2, join=True)
+    cids, variants = TP_CASES[world]
+    mp.spawn(_worker, args=(world, _free_port(), cids, variants), nprocs=world, join=True)
 
 
 def _ar_worker(rank, world, port):
