@@ -463,6 +463,276 @@ def run_decode(args, dev, world: int = 1) -> dict:
             "parallelism": "replicas (one sequence per GPU)" if world > 1 else "single GPU"}
 
 
+LLAMA_PROMPT, LLAMA_TOKENS = 512, 256
+
+
+def run_llama_prefill_decode(args, dev) -> dict:
+    """Llama-3.2-1B architecture (16 layers, hidden 2048, 32 query / 8 kv heads,
+    head_dim 64, MLP 8192, tied vocab 128256, llama3 RoPE), all-int8 synthetic
+    checkpoint: a 512-token prefill (seeded prompt ids, default_rng(7)), then
+    256 greedy tokens -- the reference's time_decode recipe (bench/decode.py:
+    26-40) on the device engine. The 256 tokens must equal quartz's own before
+    anything is timed. Prefill: CUDA-event time of one prefill pass (tensor-core
+    int8 GEMMs at M = 512, causal attention); decode: the 256 tokens from CUDA
+    graphs of 16. CPU: the oracle's decode port at context 512 and the oracle's
+    int8 GEMM on one layer's prefill shapes (M = 512), all host cores."""
+    import torch
+    import oracle
+    from oracle.decode_port import DecodePort
+    from quartz_b200 import device as qdev
+    from quartz_b200.decode import DecodeEngine
+    from quartz_b200.model import LLAMA_3P2_1B, cached_int8_weights, norm_weights, seeded_kv
+    spec = LLAMA_3P2_1B
+    with np.load(REPO / "tests" / "golden" / "golden_model.npz") as z:
+        gold = z["llama_1b_prompt512__tokens"].tolist()
+    if len(gold) < LLAMA_TOKENS:
+        raise SystemExit("the Llama-1B golden fixture holds fewer than 256 tokens")
+    prompt = np.random.default_rng(7).integers(0, spec.vocab, LLAMA_PROMPT).tolist()
+    weights = cached_int8_weights(spec)
+    eng = DecodeEngine(spec, weights, norm_weights(spec), max_ctx=LLAMA_PROMPT + LLAMA_TOKENS,
+                       max_prefill=LLAMA_PROMPT, device=dev)
+    stream = torch.cuda.current_stream()
+
+    def run_once():
+        eng.reset(0)
+        t0 = eng.prefill(prompt)
+        return [t0] + eng.generate(t0, LLAMA_TOKENS - 1, graph=True, unroll=16)
+
+    toks = run_once()
+    if toks != gold[:LLAMA_TOKENS]:
+        bad = next(i for i, (x, y) in enumerate(zip(toks, gold)) if x != y)
+        raise SystemExit(f"Llama-1B parity failed at token {bad}: {toks[bad]} != {gold[bad]}")
+    reps = 3
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    pre = []
+    for _ in range(reps):                        # prefill alone, device time
+        eng.reset(0)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        eng.prefill(prompt)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        pre.append(e0.elapsed_time(e1))
+    pre_ms = statistics.median(pre)
+    dec = []
+    for _ in range(reps):                        # the 255 graph-replayed tokens after it
+        eng.reset(0)
+        t0 = eng.prefill(prompt)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        eng.tok.fill_(t0)
+        eng.pos_dev.fill_(eng.pos)
+        n = 0
+        while n + 16 <= LLAMA_TOKENS - 1:
+            eng.replay()
+            n += 16
+        e1.record(stream)
+        torch.cuda.synchronize()
+        dec.append(e0.elapsed_time(e1) / n)
+    ms_tok = statistics.median(dec)
+    # end to end through the public calls: prompt ids in, the token list out
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        run_once()
+    e2e_s = (time.perf_counter() - t0) / reps
+    qdev.check_status(dev)
+    launches = eng._launches_per_token()
+    del eng
+    torch.cuda.empty_cache()
+    # prefill FLOPs: the int8 linears at M = 512 (2 flops per MAC) + causal attention
+    H, I, hd = spec.hidden, spec.inter, spec.head_dim
+    lin = 2 * LLAMA_PROMPT * spec.layers * (spec.qkv_rows * H + H * spec.n_heads * hd
+                                            + 2 * I * H + H * I)
+    att = 2 * 2 * spec.layers * spec.n_heads * hd * LLAMA_PROMPT * (LLAMA_PROMPT + 1) // 2
+    peak_int8 = 2 * _bf16_peak()            # int8 dense = 2x the measured bf16 GEMM rate
+    # each fp32 activation is three int8 limbs on the tensor cores: 3 int8 MACs per MAC
+    int8_tops = 3 * lin / (pre_ms * 1e-3) / 1e12
+    wbytes = spec.int8_bytes_per_token()
+    kv_mean = spec.kv_bytes_per_token(LLAMA_PROMPT + LLAMA_TOKENS // 2)
+    peak, peak_kind = _peaks()
+    achieved = (wbytes + kv_mean) / (ms_tok * 1e-3) / 1e9
+    cpu = None
+    if not args.no_cpu:
+        oracle.set_threads(_cpu_cores())
+        cfg = dict(hidden_size=H, num_hidden_layers=spec.layers, num_attention_heads=spec.n_heads,
+                   num_key_value_heads=spec.n_kv, head_dim=hd, intermediate_size=I,
+                   vocab_size=spec.vocab, rope_theta=spec.rope_theta,
+                   rope_scaling=spec.rope_scaling, tie_word_embeddings=spec.tie,
+                   rms_norm_eps=spec.eps)
+        port = DecodePort(cfg, spec.arch, {n: (q, s_) for n, q, s_ in weights},
+                          norm_weights(spec), max_ctx=LLAMA_PROMPT + 8)
+        port.load_kv(seeded_kv(spec, LLAMA_PROMPT))
+        tok = port.step(gold[0])                 # warm-up (first touch of the weights)
+        t0 = time.perf_counter()
+        for _ in range(4):
+            tok = port.step(tok)
+        cdt = (time.perf_counter() - t0) / 4
+        # prefill: the oracle's int8 GEMM on layer 0's four matmuls at M = 512
+        w = {n: (q, s_) for n, q, s_ in weights[:8]}
+        X = np.random.default_rng(3).standard_normal((LLAMA_PROMPT, H), dtype=np.float32)
+        A = np.random.default_rng(4).standard_normal((LLAMA_PROMPT, I), dtype=np.float32)
+        p0 = "model.layers.0."
+        qkv_q = np.concatenate([w[p0 + "self_attn." + n][0] for n in ("q_proj", "k_proj", "v_proj")])
+        qkv_s = np.concatenate([w[p0 + "self_attn." + n][1] for n in ("q_proj", "k_proj", "v_proj")])
+        gu_q = np.concatenate([w[p0 + "mlp.gate_proj"][0], w[p0 + "mlp.up_proj"][0]])
+        gu_s = np.concatenate([w[p0 + "mlp.gate_proj"][1], w[p0 + "mlp.up_proj"][1]])
+        t0 = time.perf_counter()
+        oracle.matmul_int8(qkv_q, qkv_s, X)
+        oracle.matmul_int8(*w[p0 + "self_attn.o_proj"], X[:, :spec.n_heads * hd])
+        oracle.matmul_int8(gu_q, gu_s, X)
+        oracle.matmul_int8(*w[p0 + "mlp.down_proj"], A)
+        layer_s = time.perf_counter() - t0
+        cpu = {"decode": {"value": round(1.0 / cdt, 2), "unit": "tok/s", "cores": oracle.threads(),
+                          "kind": "port", "sample": f"4 greedy tokens at context 512 "
+                                                    f"({cdt * 1e3:.1f} ms per token)"},
+               "prefill": {"value": round(layer_s * spec.layers * 1e3, 1), "unit": "ms",
+                           "cores": oracle.threads(), "kind": "port",
+                           "sample": "the int8 GEMMs of 1 of 16 layers at M = 512 "
+                                     f"({layer_s * 1e3:.0f} ms), times 16; attention "
+                                     "not included"}}
+    return {"workload": "llama-3.2-1b all-int8: 512-token prefill then 256 greedy tokens "
+                        "(CUDA-graph replay, 16 tokens per graph)",
+            "tokens_match_reference": True,
+            "prefill": {"ms": round(pre_ms, 3), "tokens": LLAMA_PROMPT,
+                        "tok_per_s": round(LLAMA_PROMPT / (pre_ms * 1e-3), 1),
+                        "linear_flops": lin, "attention_flops": att,
+                        "roofline": {"bound": "tensor",
+                                     "achieved": round(int8_tops, 1), "unit": "int8 TOP/s",
+                                     "peak": round(peak_int8, 1),
+                                     "frac": round(int8_tops / peak_int8, 4),
+                                     "peak_kind": "2x measured bf16 GEMM (dense int8 rate)",
+                                     "note": "whole prefill time incl. attention, norms and "
+                                             "limb splits; 3 int8 MACs per fp32 MAC"}},
+            "decode": {"value": round(1.0 / (ms_tok * 1e-3), 1), "unit": "tok/s",
+                       "us_per_token": round(ms_tok * 1e3, 2),
+                       "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                                    "unit": UNIT, "frac": round(achieved / peak, 4),
+                                    "peak_kind": peak_kind,
+                                    "bytes_per_token": wbytes + kv_mean}},
+            "e2e": {"value": round(LLAMA_TOKENS / e2e_s, 1), "unit": "tok/s",
+                    "s_per_request": round(e2e_s, 4), "h2d_bytes_per_step": 8 * LLAMA_PROMPT,
+                    "d2h_bytes_per_step": 8 * LLAMA_TOKENS,
+                    "note": "prefill(prompt ids) + generate(255): one request, prompt in, "
+                            "token list out"},
+            "cpu_baseline": cpu,
+            "gpu_launches": reps * (launches * (LLAMA_TOKENS - 1))}
+
+
+BATCH_SIZES = (2, 4, 8, 16)
+BATCH_CTX, BATCH_STEPS = 2048, 16
+
+
+def batch_parity_gate(rank: int, world: int, dev, batch: int) -> dict:
+    """The batched tensor-parallel engine at this rank count and batch
+    reproduces quartz's batched decode: the Qwen3-0.6B architecture, `batch`
+    sequences from seeded [batch, 8, 512, 128] caches, 32 greedy tokens per
+    sequence (the reference's tokens); every rank checks, the verdict is
+    all-reduced."""
+    import torch
+    from quartz_b200.model import QWEN3_0P6B, cached_int8_weights, norm_weights, seeded_kv
+    from quartz_b200.tp_decode import TPDecodeEngine
+    cid = f"qwen3_0p6b_kv512_b{batch}"
+    cases = {c["id"]: c for c in json.loads(
+        (REPO / "tests" / "golden" / "cases_model.json").read_text())["cases"]}
+    case = cases[cid]
+    with np.load(REPO / "tests" / "golden" / "golden_model.npz") as z:
+        gold = z[f"{cid}__tokens"].tolist()
+    spec = QWEN3_0P6B
+    eng = TPDecodeEngine(spec, cached_int8_weights(spec), norm_weights(spec),
+                         max_ctx=case["kv_len"] + case["steps"], max_prefill=1, device=dev,
+                         allreduce="peer", batch=batch)
+    eng.load_kv(seeded_kv(spec, case["kv_len"], batch=batch))
+    toks = eng.generate_batch(case["firsts"], case["steps"], graph=True, unroll=8)
+    eng.close()
+    del eng
+    torch.cuda.empty_cache()
+    if not _all_ranks_ok(toks == gold, world):
+        raise SystemExit(f"batched decode parity failed (batch {batch}, {world} ranks, rank {rank})")
+    return {"case": cid, "ranks": world, "batch": batch, "tokens_match_reference": True}
+
+
+def run_batch_decode(args, rank: int, world: int, dev) -> dict:
+    """Qwen3-8B all-int8 decode of M sequences in lockstep (M in {2, 4, 8, 16};
+    M = 1 is the tensor-parallel decode line), split over the ranks like the
+    single-sequence engine (heads, units, vocab rows) with the [M, H] partial
+    sums summed by the peer all-reduce kernel: every linear is the int8 GEMM on
+    M rows (tensor cores, weights read once per step), attention runs all M
+    caches in one launch. Caches hold 2048 random positions per sequence;
+    16 steps per CUDA graph. Weights are drawn on the device per shard (timing
+    does not depend on the values); each M is first gated on the reference's
+    batched tokens at the same rank count (batch_parity_gate). Strong scaling
+    over the ranks; per-GPU roofline over the rank's weight share plus its
+    share of the M caches."""
+    import torch
+    from quartz_b200.model import QWEN3_8B, norm_weights
+    from quartz_b200.tp_decode import TPDecodeEngine, random_tp_shard
+    spec = QWEN3_8B
+    stream = torch.cuda.current_stream()
+    peak, peak_kind = _peaks()
+    out = {"workload": "qwen3-8b all-int8 batched greedy decode, M sequences at context "
+                       f"{BATCH_CTX}..{BATCH_CTX + 2 * BATCH_STEPS}, CUDA-graph replay",
+           "n_gpus": world, "scaling": "strong", "rows": {}}
+    shard = random_tp_shard(spec, rank, world, dev)
+    for M in BATCH_SIZES:
+        gate = batch_parity_gate(rank, world, dev, M)
+        eng = TPDecodeEngine(spec, None, norm_weights(spec),
+                             max_ctx=BATCH_CTX + 2 * BATCH_STEPS + 8, max_prefill=1, device=dev,
+                             presharded=shard, allreduce="peer", batch=M)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(99 + rank)
+        for t in (eng.k_cache, eng.v_cache):
+            t.normal_(generator=gen)
+        eng.reset(BATCH_CTX)
+        eng.tok.copy_(torch.arange(M, device=dev) * 7919 % spec.vocab)
+        eng.capture(BATCH_STEPS)
+
+        def one_pass():
+            eng.reset(BATCH_CTX)
+            eng.replay()
+
+        for _ in range(2):
+            one_pass()
+        torch.cuda.synchronize()
+        passes = 3
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        _barrier(world)
+        e0.record(stream)
+        for _ in range(passes):
+            one_pass()
+        e1.record(stream)
+        _barrier(world)
+        ms_step = _dist_max(e0.elapsed_time(e1) / (passes * BATCH_STEPS), world)
+        launches = eng._launches_per_token()
+        eng.close()
+        del eng
+        torch.cuda.empty_cache()
+        wbytes = spec.int8_bytes_per_token()
+        kv = M * spec.kv_bytes_per_token(BATCH_CTX + BATCH_STEPS // 2)
+        per_gpu = (wbytes + kv) / world
+        achieved = per_gpu / (ms_step * 1e-3) / 1e9
+        out["rows"][f"M{M}"] = {
+            "value": round(M / (ms_step * 1e-3), 1), "unit": "tok/s",
+            "ms_per_step": round(ms_step, 4), "tokens_match_reference": True,
+            "parity_gate": gate,
+            "bytes_per_step": {"int8_weights_and_scales": wbytes, "kv_cache": kv},
+            "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "unit": UNIT, "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                         "per": "one GPU (its 1/N of the bytes)"},
+            "gpu_launches": passes * BATCH_STEPS * launches}
+    del shard
+    torch.cuda.empty_cache()
+    return out
+
+
+def _bf16_peak() -> float:
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        return float(json.loads(p.read_text())["bf16_tflops"])
+    return 1590.0
+
+
 def _log(rank: int, msg: str) -> None:
     if rank == 0:
         print(f"[bench] {msg}", file=sys.stderr, flush=True)
@@ -917,6 +1187,12 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     _log(rank, "decode done")
     tp = None if args.no_tp else run_tp(args, rank, world, dev, case)
     _log(rank, "tensor-parallel block done")
+    batch = None if args.no_batch else run_batch_decode(args, rank, world, dev)
+    _log(rank, "batched decode done")
+    llama = None
+    if not args.no_llama and world == 1:
+        llama = run_llama_prefill_decode(args, dev)
+    _log(rank, "llama prefill + decode done")
     del graphs
 
     if rank != 0:
@@ -942,7 +1218,8 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
         "cpu_baseline": cpu,
         "clocks": clk.summary() if clk else None,
         "gpu_launches": args.steps,
-        "secondary": {"mlp_body": mlp, "gemv_int4": w4, "decode": dec, "tensor_parallel": tp},
+        "secondary": {"mlp_body": mlp, "gemv_int4": w4, "decode": dec, "tensor_parallel": tp,
+                      "batched_decode": batch, "llama_prefill_decode": llama},
     }
 
 
@@ -960,6 +1237,8 @@ def main():
     ap.add_argument("--no-tp", action="store_true")
     ap.add_argument("--no-decode", action="store_true")
     ap.add_argument("--no-int4", action="store_true")
+    ap.add_argument("--no-batch", action="store_true")
+    ap.add_argument("--no-llama", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=500)
     ap.add_argument("--cpu-reps", type=int, default=30)
     args = ap.parse_args()

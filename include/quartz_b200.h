@@ -253,6 +253,30 @@ int qz_attention_decode_qkv(const float* qkv, const float* q_norm_w, const float
                             const int64_t* pos_dev, float eps, float scale, void* ws,
                             size_t ws_bytes, void* stream);
 
+/* Workspace bytes of qz_attention_decode_qkv_batch for `batch` sequences
+ * (256-byte aligned, zeroed once before first use, left ready for the next
+ * call; calls sharing it must not overlap on the GPU). */
+int qz_attention_decode_batch_workspace_bytes(int batch, int nq, int nkv, int hd, int64_t max_ctx,
+                                              int64_t* bytes);
+
+/*
+ * qz_attention_decode_qkv for `batch` sequences decoded in lockstep, the
+ * reference's batched decode step (quartz/models/common.py:79-88 with ids
+ * [B, 1]; quartz/attention.py:29-43 per batch row over its own cache,
+ * quartz/cache.py:26-46 appending each row's k/v). Sequence b reads its
+ * projection row at qkv + b * qkv_stride, appends to and attends over its
+ * caches at k_cache / v_cache + b * cache_stride ([n_kv, max_ctx, hd] each,
+ * cache_stride >= n_kv * max_ctx * hd) and writes out + b * out_stride
+ * (elements). All sequences share the position (pos0, or *pos_dev for graph
+ * replay). One launch for all sequences.
+ */
+int qz_attention_decode_qkv_batch(const float* qkv, int64_t qkv_stride, const float* q_norm_w,
+                                  const float* k_norm_w, const float* inv_freq, float* k_cache,
+                                  float* v_cache, int64_t cache_stride, float* out,
+                                  int64_t out_stride, int batch, int nq, int nkv, int hd,
+                                  int64_t max_ctx, int64_t pos0, const int64_t* pos_dev,
+                                  float eps, float scale, void* ws, size_t ws_bytes, void* stream);
+
 /* M query rows at positions pos0 .. pos0 + M - 1, each attending causally to
  * cache positions 0 .. its own (the additive mask of quartz/attention.py:15-26). */
 int qz_attention_prefill(const float* q, const float* k_cache, const float* v_cache, float* out,

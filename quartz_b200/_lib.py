@@ -50,6 +50,11 @@ SIGNATURES = {
     "qz_attention_decode_qkv": ([_vp, _vp, _vp, _vp, _vp, _vp, _vp, _int, _int, _int, _i64, _i64,
                                  _vp, ctypes.c_float, ctypes.c_float, _vp, ctypes.c_size_t, _vp],
                                 _int),
+    "qz_attention_decode_batch_workspace_bytes": ([_int, _int, _int, _int, _i64,
+                                                   ctypes.POINTER(_i64)], _int),
+    "qz_attention_decode_qkv_batch": ([_vp, _i64, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _i64, _int,
+                                       _int, _int, _int, _i64, _i64, _vp, ctypes.c_float,
+                                       ctypes.c_float, _vp, ctypes.c_size_t, _vp], _int),
     "qz_attention_decode": ([_vp, _vp, _vp, _vp, _int, _int, _int, _i64, _i64, _vp, _i64,
                              ctypes.c_float, _vp, ctypes.c_size_t, _vp], _int),
     "qz_attention_prefill": ([_vp, _vp, _vp, _vp, _i64, _int, _int, _int, _i64, _i64,

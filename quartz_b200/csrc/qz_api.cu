@@ -400,8 +400,8 @@ int launch_tc(const DeviceInfo& d, const CUtensorMap& tq, const CUtensorMap& tx,
   a.acc = a.splits > 1 ? acc : nullptr;
   if (a.acc)
     QZ_CUDA(cudaMemsetAsync(a.acc, 0, sizeof(int32_t) * qz::tc::kLimbs * a.Mpad * a.N, st));
-  const dim3 grid(static_cast<unsigned>(qz::cdiv(a.N, qz::tc::kRows)),
-                  static_cast<unsigned>(a.Mpad / MT), static_cast<unsigned>(a.splits));
+  const dim3 grid(static_cast<unsigned>(a.Mpad / MT),
+                  static_cast<unsigned>(qz::cdiv(a.N, qz::tc::kRows)), static_cast<unsigned>(a.splits));
   fn<<<grid, qz::tc::kThreads, smem, st>>>(tq, tx, a);
   QZ_CUDA(cudaGetLastError());
   if (a.acc) {
@@ -910,13 +910,14 @@ AttnLayout attn_layout(const DeviceInfo& d, int nq, int nkv, int hd, int64_t max
 }
 
 template <int E, int NR, bool QKV>
-int launch_attn_fused(const qz::dec::AttnArgs& a, int S, cudaStream_t st) {
+int launch_attn_fused(const qz::dec::AttnArgs& a, int S, cudaStream_t st, int batch = 1) {
   constexpr int smem = qz::dec::attn_fused_smem<E, NR>();
   static_assert(smem <= 48 * 1024, "fused attention shared memory above the default limit");
   // a programmatic dependent launch: the kernel hints its cache rows into L2
   // before griddepcontrol.wait and lets the next kernel launch early
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(static_cast<unsigned>(a.nkv), static_cast<unsigned>(S));
+  cfg.gridDim = dim3(static_cast<unsigned>(a.nkv), static_cast<unsigned>(S),
+                     static_cast<unsigned>(batch));
   cfg.blockDim = dim3(qz::dec::kAttnThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
@@ -931,10 +932,10 @@ int launch_attn_fused(const qz::dec::AttnArgs& a, int S, cudaStream_t st) {
 
 template <bool QKV>
 int dispatch_attn_fused(int hd, int n_rep, const qz::dec::AttnArgs& a, int S, cudaStream_t st,
-                        bool* done) {
+                        bool* done, int batch = 1) {
   *done = true;
 #define QZ_ATTN_CASE(E_, NR_) \
-  if (hd == 32 * (E_) && n_rep == (NR_)) return launch_attn_fused<E_, NR_, QKV>(a, S, st);
+  if (hd == 32 * (E_) && n_rep == (NR_)) return launch_attn_fused<E_, NR_, QKV>(a, S, st, batch);
   QZ_ATTN_CASE(2, 1) QZ_ATTN_CASE(2, 2) QZ_ATTN_CASE(2, 4) QZ_ATTN_CASE(2, 8)
   QZ_ATTN_CASE(4, 1) QZ_ATTN_CASE(4, 2) QZ_ATTN_CASE(4, 4) QZ_ATTN_CASE(4, 8)
   QZ_ATTN_CASE(8, 1) QZ_ATTN_CASE(8, 2) QZ_ATTN_CASE(8, 4)
@@ -1069,6 +1070,117 @@ int qz_attention_decode_qkv(const float* qkv, const float* q_norm_w, const float
   QZ_CUDA(cudaGetLastError());
   return attn_chunked(qs, k_cache, v_cache, out, nq, nkv, hd, max_ctx, pos_dev ? 0 : pos0 + 1,
                       pos_dev, 1, scale, part, st);
+}
+
+}  // extern "C"
+
+namespace {
+// Batched decode attention: context splits per (sequence, kv head) so that
+// all sequences together put about six CTAs on every SM (enough loads in
+// flight to stream the caches), never more than one sequence alone uses.
+int attn_splits_batch(const DeviceInfo& d, int nkv, int64_t max_ctx, int batch) {
+  const int one = attn_splits(d, nkv, max_ctx);
+  if (batch <= 1) return one;
+  const int64_t s = qz::cdiv(int64_t(6) * d.sms, int64_t(nkv) * batch);
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(s, one)));
+}
+
+// [tickets: batch * n_kv u32][the fused partials of every sequence, or, on
+// the per-sequence fallback, a whole single-sequence workspace (attn_layout)].
+// q_off is unused here.
+AttnLayout attn_layout_batch(const DeviceInfo& d, int batch, int nq, int nkv, int hd,
+                             int64_t max_ctx) {
+  AttnLayout l;
+  l.S = attn_splits_batch(d, nkv, max_ctx, batch);
+  auto al = [](int64_t b) { return ((b + 255) / 256) * 256; };
+  const int64_t fused = int64_t(batch) * nkv * l.S * (nq / nkv) * (hd + 2) * 4;
+  const AttnLayout one = attn_layout(d, nq, nkv, hd, max_ctx);
+  l.part_off = al(int64_t(batch) * nkv * 4);
+  l.q_off = l.part_off;
+  l.total = l.part_off + std::max(al(fused), one.total);
+  return l;
+}
+}  // namespace
+
+extern "C" {
+
+int qz_attention_decode_batch_workspace_bytes(int batch, int nq, int nkv, int hd, int64_t max_ctx,
+                                              int64_t* bytes) {
+  if (!bytes || batch < 1 || nq < 1 || nkv < 1 || nq % nkv || hd < 1 || max_ctx < 1)
+    return fail(QZ_ERR_INVALID, "qz_attention_decode_batch_workspace_bytes: bad arguments");
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  *bytes = attn_layout_batch(*d, batch, nq, nkv, hd, max_ctx).total;
+  return QZ_OK;
+}
+
+int qz_attention_decode_qkv_batch(const float* qkv, int64_t qkv_stride, const float* q_norm_w,
+                                  const float* k_norm_w, const float* inv_freq, float* k_cache,
+                                  float* v_cache, int64_t cache_stride, float* out,
+                                  int64_t out_stride, int batch, int nq, int nkv, int hd,
+                                  int64_t max_ctx, int64_t pos0, const int64_t* pos_dev,
+                                  float eps, float scale, void* ws, size_t ws_bytes,
+                                  void* stream) {
+  if (int rc = check_heads(nq, nkv, hd, "qz_attention_decode_qkv_batch")) return rc;
+  if (batch < 1 || max_ctx < 1) return fail(QZ_ERR_INVALID, "qz_attention_decode_qkv_batch: bad batch or max_ctx");
+  const int64_t rows = static_cast<int64_t>(nq + 2 * nkv) * hd;
+  if (qkv_stride < rows || out_stride < static_cast<int64_t>(nq) * hd ||
+      cache_stride < static_cast<int64_t>(nkv) * max_ctx * hd)
+    return fail(QZ_ERR_INVALID, "qz_attention_decode_qkv_batch: a stride is shorter than its row");
+  if (!pos_dev && (pos0 < 0 || pos0 >= max_ctx))
+    return fail(QZ_ERR_INVALID, "qz_attention_decode_qkv_batch: position outside the cache");
+  if (!qkv || !inv_freq || !k_cache || !v_cache || !out || !ws)
+    return fail(QZ_ERR_INVALID, "qz_attention_decode_qkv_batch: null pointer");
+  if ((q_norm_w == nullptr) != (k_norm_w == nullptr))
+    return fail(QZ_ERR_INVALID, "qz_attention_decode_qkv_batch: pass both norm weights or neither");
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  const AttnLayout L = attn_layout_batch(*d, batch, nq, nkv, hd, max_ctx);
+  if (static_cast<int64_t>(ws_bytes) < L.total || !aligned_to(ws, 256))
+    return fail(QZ_ERR_INVALID,
+                "qz_attention_decode_qkv_batch: workspace too small or not 256-byte aligned");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  char* w = static_cast<char*>(ws);
+  const bool strides16 = qkv_stride % 4 == 0 && cache_stride % 4 == 0;
+  if (aligned16(qkv) && aligned16(k_cache) && aligned16(v_cache) && strides16) {
+    qz::dec::AttnArgs a{};
+    a.in = qkv;
+    a.qn_w = q_norm_w;
+    a.kn_w = k_norm_w;
+    a.inv_freq = inv_freq;
+    a.kc = k_cache;
+    a.vc = v_cache;
+    a.out = out;
+    a.part = reinterpret_cast<float*>(w + L.part_off);
+    a.tickets = reinterpret_cast<unsigned*>(w);
+    a.len_dev = pos_dev;
+    a.len0 = pos_dev ? 0 : pos0;
+    a.len_off = 1;
+    a.max_ctx = max_ctx;
+    a.nq = nq;
+    a.nkv = nkv;
+    a.scale = scale;
+    a.eps = eps;
+    a.in_bstride = qkv_stride;
+    a.kv_bstride = cache_stride;
+    a.out_bstride = out_stride;
+    bool done = false;
+    if (int rc = dispatch_attn_fused<true>(hd, nq / nkv, a, L.S, st, &done, batch)) return rc;
+    if (done) return QZ_OK;
+  }
+  // other shapes: one sequence after the other through the single-sequence
+  // path (stream-ordered, so they share one single-sequence workspace placed
+  // after the batched tickets, which stay zero)
+  void* ws1 = w + L.part_off;
+  const size_t ws1_bytes = ws_bytes - static_cast<size_t>(L.part_off);
+  for (int b = 0; b < batch; ++b) {
+    if (int rc = qz_attention_decode_qkv(qkv + b * qkv_stride, q_norm_w, k_norm_w, inv_freq,
+                                         k_cache + b * cache_stride, v_cache + b * cache_stride,
+                                         out + b * out_stride, nq, nkv, hd, max_ctx, pos0, pos_dev,
+                                         eps, scale, ws1, ws1_bytes, stream))
+      return rc;
+  }
+  return QZ_OK;
 }
 
 }  // extern "C"

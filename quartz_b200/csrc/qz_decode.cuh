@@ -527,6 +527,11 @@ struct AttnArgs {
   int64_t len0, len_off, max_ctx;
   int nq, nkv;
   float scale, eps;
+  // Sequences decoded in lockstep (grid z): sequence b reads in + b * in_bstride,
+  // its caches at kc / vc + b * kv_bstride and writes out + b * out_bstride
+  // (elements); its partials and tickets follow sequence b-1's. Zero strides
+  // with one sequence are the single-sequence launch.
+  int64_t in_bstride, kv_bstride, out_bstride;
 };
 
 constexpr int kAttnThreads = 256;
@@ -600,7 +605,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_fused_kernel(AttnArg
   float* red = qs + NR * HD;                           // [warps][NR][HD + 2]
   __shared__ unsigned s_last;
   const int g = blockIdx.x, c = blockIdx.y, S = gridDim.y;
+  const int64_t b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const float* in = a.in + b * a.in_bstride;
+  float* const kc = a.kc + b * a.kv_bstride;
+  float* const vc = a.vc + b * a.kv_bstride;
   const int64_t kv_off = static_cast<int64_t>(g) * a.max_ctx * HD;
   // Launched as a programmatic dependent of the projection that writes `in`:
   // the next kernel may launch now (it waits for this grid's completion),
@@ -618,7 +627,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_fused_kernel(AttnArg
     for (int64_t i = threadIdx.x; i < (p1 - p0) * 2 * kLines; i += kAttnThreads) {
       const int64_t t = p0 + i / (2 * kLines);
       const int j = static_cast<int>(i % (2 * kLines));
-      prefetch_l2((j < kLines ? a.kc : a.vc) + kv_off + t * HD + (j % kLines) * 32);
+      prefetch_l2((j < kLines ? kc : vc) + kv_off + t * HD + (j % kLines) * 32);
     }
   }
   pdl_wait();
@@ -631,13 +640,15 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_fused_kernel(AttnArg
   // the append happens only for a position inside the cache
   const int64_t t_raw = (a.len_dev ? *a.len_dev : a.len0) + a.len_off;
   const bool append = QKV && t_raw >= 1 && t_raw <= a.max_ctx;
-  float* pbase = a.part + (static_cast<int64_t>(g) * S + c) * NR * (HD + 2);
+  // this sequence's partials [nkv][S][NR][HD + 2] follow the previous one's
+  float* const part = a.part + b * static_cast<int64_t>(a.nkv) * S * NR * (HD + 2);
+  float* pbase = part + (static_cast<int64_t>(g) * S + c) * NR * (HD + 2);
 
   if (t0 < t1) {
     // queries of this group (and, in the owning CTA, the new key/value)
     for (int r = warp; r < NR; r += kAttnWarps) {
       float x[E];
-      load_vec<E>(a.in + static_cast<int64_t>(g * NR + r) * HD + lane * E, x);
+      load_vec<E>(in + static_cast<int64_t>(g * NR + r) * HD + lane * E, x);
       if constexpr (QKV) norm_rope<E>(x, a.qn_w, a.inv_freq, pos, a.eps, lane);
 #pragma unroll
       for (int e = 0; e < E; ++e) qs[r * HD + lane * E + e] = x[e];
@@ -645,11 +656,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_fused_kernel(AttnArg
     if constexpr (QKV) {
       if (append && t0 <= pos && pos < t1 && warp == NR % kAttnWarps) {
         float k[E], v[E];
-        load_vec<E>(a.in + static_cast<int64_t>(a.nq + g) * HD + lane * E, k);
-        load_vec<E>(a.in + static_cast<int64_t>(a.nq + a.nkv + g) * HD + lane * E, v);
+        load_vec<E>(in + static_cast<int64_t>(a.nq + g) * HD + lane * E, k);
+        load_vec<E>(in + static_cast<int64_t>(a.nq + a.nkv + g) * HD + lane * E, v);
         norm_rope<E>(k, a.kn_w, a.inv_freq, pos, a.eps, lane);
-        store_vec<E>(a.kc + kv_off + pos * HD + lane * E, k);
-        store_vec<E>(a.vc + kv_off + pos * HD + lane * E, v);
+        store_vec<E>(kc + kv_off + pos * HD + lane * E, k);
+        store_vec<E>(vc + kv_off + pos * HD + lane * E, v);
       }
     }
     __syncthreads();   // queries in shared memory; the appended row visible to the CTA
@@ -673,8 +684,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_fused_kernel(AttnArg
         const int64_t t = tb + u * kAttnWarps;
         ok[u] = t < t1;
         if (ok[u]) {
-          load_vec<E>(a.kc + kv_off + t * HD + lane * E, kr[u]);
-          load_vec<E>(a.vc + kv_off + t * HD + lane * E, vr[u]);
+          load_vec<E>(kc + kv_off + t * HD + lane * E, kr[u]);
+          load_vec<E>(vc + kv_off + t * HD + lane * E, vr[u]);
         } else {
 #pragma unroll
           for (int e = 0; e < E; ++e) kr[u][e] = vr[u][e] = 0.f;
@@ -750,17 +761,18 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_fused_kernel(AttnArg
 
   // the last CTA of kv head g merges the S partials of its query heads
   __syncthreads();
+  unsigned* const tickets = a.tickets + b * a.nkv;
   if (threadIdx.x == 0) {
     __threadfence();
-    s_last = atomicAdd(a.tickets + g, 1u) == static_cast<unsigned>(S - 1);
+    s_last = atomicAdd(tickets + g, 1u) == static_cast<unsigned>(S - 1);
   }
   __syncthreads();
   if (!s_last) return;
   __threadfence();
-  const float* gbase = a.part + static_cast<int64_t>(g) * S * NR * (HD + 2);
-  merge_partials<HD, NR, kAttnThreads>(gbase, S, a.out + static_cast<int64_t>(g) * NR * HD, red,
+  const float* gbase = part + static_cast<int64_t>(g) * S * NR * (HD + 2);
+  merge_partials<HD, NR, kAttnThreads>(gbase, S, a.out + b * a.out_bstride + static_cast<int64_t>(g) * NR * HD, red,
                                        threadIdx.x, [] { __syncthreads(); });
-  if (threadIdx.x == 0) a.tickets[g] = 0u;
+  if (threadIdx.x == 0) tickets[g] = 0u;
 }
 
 template <int E, int NR>

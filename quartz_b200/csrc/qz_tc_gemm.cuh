@@ -234,8 +234,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 1);
   __shared__ int s_err;
 
-  const int64_t n0 = static_cast<int64_t>(blockIdx.x) * kRows;
-  const int64_t m0 = static_cast<int64_t>(blockIdx.y) * MT;
+  // grid (token tiles, weight tiles, K splits): the token tiles that share a
+  // 128-row weight panel are adjacent in launch order, so they run at the
+  // same time and the panel comes from DRAM once and from L2 for the rest
+  const int64_t n0 = static_cast<int64_t>(blockIdx.y) * kRows;
+  const int64_t m0 = static_cast<int64_t>(blockIdx.x) * MT;
   const int nk_all = static_cast<int>(cdiv(a.K, kKBytes));
   // this CTA's K blocks: [kb0, kb0 + nk)
   const int kb0 = static_cast<int>(static_cast<int64_t>(nk_all) * blockIdx.z / a.splits);

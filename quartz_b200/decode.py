@@ -123,8 +123,19 @@ class DecodeEngine:
 
     def __init__(self, spec: ModelSpec, int8_weights: Mapping | Iterable, norms: Mapping,
                  *, max_ctx: int, max_prefill: int = 512, device=None,
-                 persistent: bool = False, fold_norms: bool = True):
+                 persistent: bool = False, fold_norms: bool = True, batch: int = 1):
+        """batch: sequences decoded in lockstep (quartz's decode_logits on [B, 1]
+        ids, quartz/models/common.py:79-88): every step runs B rows through the
+        int8 GEMMs (M = B, quartz/kernels/int8.py:66-87, 106-107), the per-op
+        MLP (quartz/quantize.py:112-114) and a batched attention over B caches
+        sharing one position. batch > 1 decodes through generate_batch and has
+        no prefill (sequences start from a loaded cache)."""
         self.spec = spec
+        self.batch = int(batch)
+        if self.batch < 1:
+            raise ValueError("batch must be >= 1")
+        if self.batch > 1:
+            persistent = False
         self.dev = torch.device("cuda", qd.ensure_device(device))
         dev = self.dev
         self.lib = _lib.load()
@@ -194,9 +205,12 @@ class DecodeEngine:
 
         # KV cache and activation buffers
         f32 = dict(dtype=torch.float32, device=dev)
-        self.k_cache = torch.zeros((S.layers, S.n_kv, self.max_ctx, hd), **f32)
-        self.v_cache = torch.zeros((S.layers, S.n_kv, self.max_ctx, hd), **f32)
-        Mx = self.max_prefill
+        B = self.batch
+        cache_shape = ((S.layers, S.n_kv, self.max_ctx, hd) if B == 1 else
+                       (S.layers, B, S.n_kv, self.max_ctx, hd))
+        self.k_cache = torch.zeros(cache_shape, **f32)
+        self.v_cache = torch.zeros(cache_shape, **f32)
+        Mx = max(self.max_prefill, B)
         self.h_a = torch.zeros((Mx, H), **f32)
         self.h_b = torch.zeros((Mx, H), **f32)
         self.xn = torch.zeros((Mx, H), **f32)
@@ -206,9 +220,9 @@ class DecodeEngine:
         self.gu = torch.zeros((Mx, 2 * S.inter), **f32) if Mx > 1 else None
         self.act = torch.zeros((Mx, S.inter), **f32) if Mx > 1 else None
         self.abuf = torch.zeros(S.inter, **f32)
-        self.logits = torch.zeros(S.vocab, **f32)
-        self.keys = torch.zeros(8, dtype=torch.int64, device=dev)
-        self.tok = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.logits = torch.zeros(S.vocab, **f32) if B == 1 else torch.zeros((B, S.vocab), **f32)
+        self.keys = torch.zeros(max(8, B), dtype=torch.int64, device=dev)
+        self.tok = torch.zeros(B, dtype=torch.int64, device=dev)
         self.ids = torch.zeros(Mx, dtype=torch.int64, device=dev)
         self.pos_dev = torch.zeros(1, dtype=torch.int64, device=dev)
         self.pos = 0
@@ -216,13 +230,20 @@ class DecodeEngine:
                                   device=dev)
         b = ctypes.c_int64(0)
         with torch.cuda.device(dev):
-            _lib.check(self.lib.qz_attention_decode_workspace_bytes(
-                S.n_heads, S.n_kv, hd, self.max_ctx, ctypes.byref(b)))
+            if B == 1:
+                _lib.check(self.lib.qz_attention_decode_workspace_bytes(
+                    S.n_heads, S.n_kv, hd, self.max_ctx, ctypes.byref(b)))
+            else:
+                _lib.check(self.lib.qz_attention_decode_batch_workspace_bytes(
+                    B, S.n_heads, S.n_kv, hd, self.max_ctx, ctypes.byref(b)))
         self.attn_ws = torch.zeros(b.value, dtype=torch.uint8, device=dev)
         self.gemm_ws = None
         if Mx > 1:
             need = 0
-            for N, K in ((S.qkv_rows, H), (H, S.n_heads * hd), (2 * S.inter, H), (H, S.inter)):
+            shapes = [(S.qkv_rows, H), (H, S.n_heads * hd), (2 * S.inter, H), (H, S.inter)]
+            if B > 1:
+                shapes.append((self.lm_q.shape[0], H))      # the lm_head runs M = B rows
+            for N, K in shapes:
                 b = ctypes.c_int64(0)
                 _lib.check(self.lib.qz_gemm_w8_workspace_bytes(Mx, N, K, ctypes.byref(b)))
                 need = max(need, b.value)
@@ -278,23 +299,28 @@ class DecodeEngine:
         self.pos_dev.fill_(self.pos)
 
     def load_kv(self, kv: Iterable) -> None:
-        """Fill the cache from per-layer (K, V) [n_kv, T, head_dim] arrays and set
-        the position to T (the prefilled-cache start, like calling quartz's
-        update_and_fetch once per layer, quartz/cache.py:26-46)."""
+        """Fill the cache from per-layer (K, V) [n_kv, T, head_dim] arrays
+        ([batch, n_kv, T, head_dim] for a batched engine) and set the position
+        to T (the prefilled-cache start, like calling quartz's update_and_fetch
+        once per layer, quartz/cache.py:26-46)."""
         T = None
         n = 0
+        B = self.batch
         for i, (k, v) in enumerate(kv):
             k = torch.as_tensor(np.ascontiguousarray(k, np.float32))
             v = torch.as_tensor(np.ascontiguousarray(v, np.float32))
-            t = k.shape[1]
+            t = k.shape[-2]
             if T is None:
                 T = t
-            if k.shape != (self.spec.n_kv, T, self.spec.head_dim) or v.shape != k.shape:
-                raise ValueError("K/V must be [n_kv, T, head_dim] with one T for all layers")
+            want = (self.spec.n_kv, T, self.spec.head_dim) if B == 1 else \
+                (B, self.spec.n_kv, T, self.spec.head_dim)
+            if tuple(k.shape) != want or v.shape != k.shape:
+                raise ValueError("K/V must be [n_kv, T, head_dim] ([batch, n_kv, T, head_dim] "
+                                 "for a batched engine) with one T for all layers")
             if T > self.max_ctx:
                 raise ValueError("prefilled context exceeds max_ctx")
-            self.k_cache[i, :, :T].copy_(k)
-            self.v_cache[i, :, :T].copy_(v)
+            self.k_cache[i, ..., :T, :].copy_(k)
+            self.v_cache[i, ..., :T, :].copy_(v)
             n += 1
         if n != self.spec.layers:
             raise ValueError(f"expected K/V for {self.spec.layers} layers, got {n}")
@@ -307,6 +333,8 @@ class DecodeEngine:
     def _decode_ops(self, st: int) -> None:
         """One token at position *pos_dev: reads self.tok, writes self.tok and
         advances pos_dev. Every call is a libquartz_b200 launch on stream st."""
+        if self.batch > 1:
+            return self._decode_ops_batch(st)
         S, lib, chk = self.spec, self.lib, _lib.check
         H, hd, nq, nkv = S.hidden, S.head_dim, S.n_heads, S.n_kv
         p = lambda t: t.data_ptr()  # noqa: E731
@@ -365,7 +393,69 @@ class DecodeEngine:
         chk(lib.qz_argmax(p(self.logits), 1, S.vocab, p(self.keys), p(self.tok), p(self.pos_dev),
                           1, st))
 
+    def _batch_layer_attn(self, li: int, L, st: int) -> None:
+        """RMSNorm, q/k/v GEMM and the batched attention of layer li for the
+        B rows in h_a; the attention output goes to ao."""
+        S, lib, chk = self.spec, self.lib, _lib.check
+        B, H, hd, nq, nkv = self.batch, S.hidden, S.head_dim, S.n_heads, S.n_kv
+        p = lambda t: t.data_ptr()  # noqa: E731
+        ws, wsb = p(self.gemm_ws), self.gemm_ws.numel()
+        chk(lib.qz_rmsnorm(p(self.h_a), p(L.in_w), p(self.xn), B, H, S.eps, st))
+        chk(lib.qz_gemm_w8_ws(p(L.qkv_q), p(L.qkv_s), L.qkv_s.shape[1], p(self.xn), p(self.qkv),
+                              B, S.qkv_rows, H, None, ws, wsb, st))
+        chk(lib.qz_attention_decode_qkv_batch(
+            p(self.qkv), self.qkv.shape[1], qd._ptr(L.qn_w), qd._ptr(L.kn_w), p(self.inv_freq),
+            p(self.k_cache[li]), p(self.v_cache[li]), nkv * self.max_ctx * hd, p(self.ao),
+            self.ao.shape[1], B, nq, nkv, hd, self.max_ctx, 0, p(self.pos_dev), S.eps,
+            self.attn_scale, p(self.attn_ws), self.attn_ws.numel(), st))
+
+    def _decode_ops_batch(self, st: int) -> None:
+        """One step of B sequences at position *pos_dev: reads tok [B], writes
+        tok [B] and advances pos_dev. quartz's batched decode step: every
+        linear is the int8 GEMM on B rows (w8a32_gemm), the MLP the per-op
+        path with the clipped SiLU (quartz/quantize.py:112-114)."""
+        S, lib, chk = self.spec, self.lib, _lib.check
+        B, H, hd, nq, I = self.batch, S.hidden, S.head_dim, S.n_heads, S.inter
+        p = lambda t: t.data_ptr()  # noqa: E731
+        h_a, h_b, xn = p(self.h_a), p(self.h_b), p(self.xn)
+        ws, wsb = p(self.gemm_ws), self.gemm_ws.numel()
+        chk(lib.qz_embed_gather(p(self.embed_q), p(self.embed_s), self.embed_s.shape[1],
+                                p(self.tok), B, S.vocab, H, h_a, st))
+        for li, L in enumerate(self.layers):
+            self._batch_layer_attn(li, L, st)
+            chk(lib.qz_gemm_w8_ws(p(L.o_q), p(L.o_s), L.o_s.shape[1], p(self.ao), h_b, B, H,
+                                  nq * hd, h_a, ws, wsb, st))
+            chk(lib.qz_rmsnorm(h_b, p(L.post_w), xn, B, H, S.eps, st))
+            chk(lib.qz_gemm_w8_ws(p(L.gu_q), p(L.gu_s), L.gu_s.shape[1], xn, p(self.gu), B,
+                                  2 * I, H, None, ws, wsb, st))
+            chk(lib.qz_silu_mul(p(self.gu), p(self.act), B, I, st))
+            chk(lib.qz_gemm_w8_ws(p(L.down_q), p(L.down_s), L.down_s.shape[1], p(self.act), h_a,
+                                  B, H, I, h_b, ws, wsb, st))
+        chk(lib.qz_rmsnorm(h_a, p(self.norm_w), xn, B, H, S.eps, st))
+        V = self.lm_q.shape[0]
+        chk(lib.qz_gemm_w8_ws(p(self.lm_q), p(self.lm_s), self.lm_s.shape[1], xn,
+                              p(self.logits), B, V, H, None, ws, wsb, st))
+        chk(lib.qz_argmax(p(self.logits), B, V, p(self.keys), p(self.tok), p(self.pos_dev), 1,
+                          st))
+
+    def _gemm_launches(self, M: int, N: int) -> int:
+        """Kernels one qz_gemm_w8_ws call launches for M > 1 rows on the tensor
+        path: the activation split and the GEMM, plus the split-K finish when
+        the output tiles alone leave SMs idle."""
+        sms = torch.cuda.get_device_properties(self.dev).multi_processor_count
+        m16 = -(-M // 16) * 16
+        mt = 128 if m16 >= 128 else (64 if m16 > 32 else m16)
+        tiles = -(-N // 128) * (-(-M // mt))
+        return 3 if tiles < sms else 2
+
     def _launches_per_token(self) -> int:
+        if self.batch > 1:
+            # per step (B tokens): embed, per layer (rmsnorm, qkv GEMM, attention, o GEMM,
+            # rmsnorm, gate/up GEMM, silu, down GEMM), final rmsnorm, lm_head GEMM, argmax x2
+            S, B, g = self.spec, self.batch, self._gemm_launches
+            per_layer = (4 + g(B, S.qkv_rows) + g(B, S.hidden) + g(B, 2 * S.inter)
+                         + g(B, S.hidden))
+            return 1 + per_layer * S.layers + 1 + g(B, self.lm_q.shape[0]) + 2
         if self.persistent:
             return 4   # decode_layers, lm_head GEMV, argmax + finish
         # embed + per layer (qkv with its norm, attention, o, mlp with its norm) + lm with
@@ -385,6 +475,8 @@ class DecodeEngine:
     def prefill(self, ids: Iterable[int]) -> int:
         """Run the prompt ids at the current position; return the greedy next token
         (quartz/generate.py:50 then quartz/models/common.py:69-78 on the last row)."""
+        if self.batch > 1:
+            raise ValueError("a batched engine decodes through generate_batch")
         ids = [int(t) for t in ids]
         M = len(ids)
         S = self.spec
@@ -438,6 +530,8 @@ class DecodeEngine:
 
     def decode(self, token: int) -> int:
         """One eager decode step from `token`; returns the greedy next token."""
+        if self.batch > 1:
+            raise ValueError("a batched engine decodes through generate_batch")
         if not 0 <= token < self.spec.vocab:
             raise ValueError("token id outside the vocabulary")
         if self.pos >= self.max_ctx:
@@ -454,7 +548,8 @@ class DecodeEngine:
         its token into a device history slot) into one CUDA graph."""
         steps = max(1, int(steps))
         self._graph = None
-        self.hist = torch.zeros(steps, dtype=torch.int64, device=self.dev)
+        self.hist = torch.zeros(steps if self.batch == 1 else (steps, self.batch),
+                                dtype=torch.int64, device=self.dev)
         # One eager step first, so every launch path (kernel attributes, the
         # cooperative-launch form) is settled outside the capture. It writes the
         # cache row at the current position, which the next real step rewrites;
@@ -473,7 +568,7 @@ class DecodeEngine:
                 st = side.cuda_stream
                 for i in range(steps):
                     self._decode_ops(st)
-                    self.hist[i:i + 1].copy_(self.tok)
+                    self.hist[i:i + 1].copy_(self.tok.view(1, -1) if self.batch > 1 else self.tok)
         torch.cuda.current_stream(self.dev).wait_stream(side)
         self._graph = g
         self._graph_steps = steps
@@ -494,6 +589,8 @@ class DecodeEngine:
         """Greedy tokens after feeding `first` at the current position: the
         decode loop of quartz/generate.py:52-58 (without EOS handling), `steps`
         tokens, the first being the argmax of `first`'s logits."""
+        if self.batch > 1:
+            raise ValueError("a batched engine decodes through generate_batch")
         if steps <= 0:
             return []
         if self.pos + steps > self.max_ctx:
@@ -520,6 +617,41 @@ class DecodeEngine:
         while done < steps:
             self._decode_ops(st)
             out[done:done + 1].copy_(self.tok)
+            self.pos += 1
+            done += 1
+        return out.cpu().tolist()
+
+    def generate_batch(self, firsts, steps: int, *, graph: bool = True, unroll: int = 8
+                       ) -> list[list[int]]:
+        """Greedy tokens of the B sequences after feeding firsts[b] to sequence b
+        at the current (shared) position: `steps` rows of B tokens, row 0 the
+        argmax of each sequence's logits for its first token."""
+        firsts = [int(t) for t in firsts]
+        if len(firsts) != self.batch:
+            raise ValueError(f"expected {self.batch} first tokens, got {len(firsts)}")
+        if any(t < 0 or t >= self.spec.vocab for t in firsts):
+            raise ValueError("token id outside the vocabulary")
+        if steps <= 0:
+            return []
+        if self.pos + steps > self.max_ctx:
+            raise ValueError("generation would overflow the cache")
+        self.tok.copy_(torch.tensor(firsts, dtype=torch.int64))
+        self.pos_dev.fill_(self.pos)
+        st = self._stream()
+        out = torch.empty((steps, self.batch), dtype=torch.int64, device=self.dev)
+        done = 0
+        if graph:
+            if self._graph is None or self._graph_steps != unroll:
+                self.capture(unroll)
+                self.tok.copy_(torch.tensor(firsts, dtype=torch.int64))
+            self.pos_dev.fill_(self.pos)
+            while steps - done >= self._graph_steps:
+                h = self.replay()
+                out[done:done + self._graph_steps].copy_(h.view(self._graph_steps, self.batch))
+                done += self._graph_steps
+        while done < steps:
+            self._decode_ops(st)
+            out[done].copy_(self.tok)
             self.pos += 1
             done += 1
         return out.cpu().tolist()

@@ -224,14 +224,15 @@ def norm_weights(spec: ModelSpec) -> dict[str, np.ndarray]:
     return out
 
 
-def seeded_kv(spec: ModelSpec, length: int, seed: int = 99
+def seeded_kv(spec: ModelSpec, length: int, seed: int = 99, batch: int | None = None
               ) -> Iterator[tuple[np.ndarray, np.ndarray]]:
     """Per layer, (K, V) fp32 [n_kv, length, head_dim] of N(0, 1) draws from one
     default_rng(seed), K before V, layer by layer (the prefilled-cache start of
-    the decode workload)."""
+    the decode workload). With `batch` B, per layer [B, n_kv, length,
+    head_dim] draws (the caches of B sequences decoded in lockstep)."""
     rng = np.random.default_rng(seed)
-    shape = (1, spec.n_kv, length, spec.head_dim)
+    shape = (batch or 1, spec.n_kv, length, spec.head_dim)
     for _ in range(spec.layers):
         k = rng.standard_normal(shape, dtype=np.float32)
         v = rng.standard_normal(shape, dtype=np.float32)
-        yield k[0], v[0]
+        yield (k[0], v[0]) if batch is None else (k, v)

@@ -103,7 +103,7 @@ class TPDecodeEngine(DecodeEngine):
 
     def __init__(self, spec: ModelSpec, int8_weights: Mapping | Iterable | None, norms: Mapping,
                  *, group=None, max_ctx: int, max_prefill: int = 512, device=None,
-                 presharded=None, allreduce: str = "fused"):
+                 presharded=None, allreduce: str = "fused", batch: int = 1):
         """int8_weights: the full checkpoint (every rank slices its part with
         tp_shard), or None with presharded = tp_shard(...)'s result for this
         rank (arrays may be torch tensors already on the device).
@@ -112,7 +112,10 @@ class TPDecodeEngine(DecodeEngine):
         their epilogues and the following RMSNorm sums them as it reads
         (no collective launches); "peer": the peer-memory all-reduce kernel
         (quartz_b200.comm); "nccl": the process group's all-reduce. Prefill's
-        [M, H] sums always use NCCL."""
+        [M, H] sums always use NCCL.
+        batch: sequences decoded in lockstep (DecodeEngine's batch); their
+        [B, H] partial sums go through the peer all-reduce kernel ("fused" and
+        "peer") or NCCL ("nccl"), since the in-kernel push serves one row."""
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -120,21 +123,24 @@ class TPDecodeEngine(DecodeEngine):
         local, w, (lq, ls, vlo, vhi) = (presharded if presharded is not None else
                                         tp_shard(spec, int8_weights, self.rank, self.world))
         super().__init__(local, w, norms, max_ctx=max_ctx, max_prefill=max_prefill,
-                         device=device, persistent=False)
+                         device=device, persistent=False, batch=batch)
         self.lm_q = _to_dev(lq, torch.int8, self.dev)
         self.lm_s = _to_dev(ls, torch.float32, self.dev)
         self.vlo, self.vhi = vlo, vhi
-        self.logits = torch.zeros(max(vhi - vlo, 1), dtype=torch.float32, device=self.dev)
-        self.ltok = torch.zeros(1, dtype=torch.int64, device=self.dev)
-        self.pair = torch.zeros((1, 2), dtype=torch.float64, device=self.dev)
-        self.pairs = torch.zeros((self.world, 2), dtype=torch.float64, device=self.dev)
+        B = self.batch
+        n_local = max(vhi - vlo, 1)
+        self.logits = torch.zeros(n_local if B == 1 else (B, n_local), dtype=torch.float32,
+                                  device=self.dev)
+        self.ltok = torch.zeros(B, dtype=torch.int64, device=self.dev)
+        self.pair = torch.zeros((B, 2), dtype=torch.float64, device=self.dev)
+        self.pairs = torch.zeros((self.world * B, 2), dtype=torch.float64, device=self.dev)
         if allreduce not in ("fused", "peer", "nccl"):
             raise ValueError("allreduce must be 'fused', 'peer' or 'nccl'")
         self.peer = None
-        self.fused_ar = allreduce == "fused" and self.world > 1
+        self.fused_ar = allreduce == "fused" and self.world > 1 and B == 1
         if allreduce in ("fused", "peer") and self.world > 1:
             from .comm import PeerAllReduce
-            self.peer = PeerAllReduce(self.spec.hidden, group=group, device=self.dev)
+            self.peer = PeerAllReduce(self.spec.hidden * B, group=group, device=self.dev)
         if self.fused_ar:
             self.peer_sum = ctypes.byref(self.peer.ps)
 
@@ -150,7 +156,9 @@ class TPDecodeEngine(DecodeEngine):
         """Per layer full (K, V) [n_kv, T, head_dim]: this rank keeps its kv heads."""
         n = self.spec.n_kv
         lo = self.rank * n
-        super().load_kv((np.asarray(k)[lo:lo + n], np.asarray(v)[lo:lo + n]) for k, v in kv)
+        ax = 0 if self.batch == 1 else 1      # batched caches are [B, n_kv, T, hd]
+        sl = (slice(None),) * ax + (slice(lo, lo + n),)
+        super().load_kv((np.asarray(k)[sl], np.asarray(v)[sl]) for k, v in kv)
 
     # -------------------------------------------------------------- collectives
     def _all_reduce(self, t: torch.Tensor) -> None:
@@ -163,19 +171,22 @@ class TPDecodeEngine(DecodeEngine):
         """Greedy token over the vocab shards: local argmax, then one all-gather
         of (max value, global index) and the lowest index among the maxima."""
         S, lib, chk = self.spec, self.lib, _lib.check
+        B = self.batch
         n_local = self.vhi - self.vlo
         if n_local > 0:
-            chk(lib.qz_argmax(self.logits.data_ptr(), 1, n_local, self.keys.data_ptr(),
+            chk(lib.qz_argmax(self.logits.data_ptr(), B, n_local, self.keys.data_ptr(),
                               self.ltok.data_ptr(), None, 0, st))
-            self.pair[:, 0].copy_(self.logits.index_select(0, self.ltok))
+            self.pair[:, 0].copy_(self.logits.view(B, -1).gather(1, self.ltok.view(B, 1))[:, 0])
             self.pair[:, 1].copy_(self.ltok + self.vlo)
         else:
             self.pair[:, 0].fill_(float("-inf"))
             self.pair[:, 1].fill_(float(S.vocab))
         dist.all_gather_into_tensor(self.pairs, self.pair, group=self.group)
-        vals, idx = self.pairs[:, 0], self.pairs[:, 1]
-        cand = torch.where(vals == vals.max(), idx, torch.full_like(idx, float("inf")))
-        self.tok.copy_(cand.min().to(torch.int64).reshape(1))
+        vals = self.pairs[:, 0].view(self.world, B)
+        idx = self.pairs[:, 1].view(self.world, B)
+        best = vals.max(dim=0, keepdim=True).values
+        cand = torch.where(vals == best, idx, torch.full_like(idx, float("inf")))
+        self.tok.copy_(cand.min(dim=0).values.to(torch.int64))
         self.pos_dev.add_(pos_step)
 
     # ------------------------------------------------------------- the token
@@ -217,7 +228,41 @@ class TPDecodeEngine(DecodeEngine):
                                p(self.logits), n_local, H, None, st))
         self._pick_token(st, 1)
 
+    def _decode_ops_batch(self, st: int) -> None:
+        """One step of the B sequences on this rank's shard: every rank runs its
+        heads and units over all B rows; the o-projection and down-projection
+        [B, H] partials (rank 0 carrying the residual) are summed by one
+        all-reduce each; the lm_head by vocab rows with a per-row pick."""
+        S, lib, chk = self.spec, self.lib, _lib.check
+        B, H, hd, nq, I = self.batch, S.hidden, S.head_dim, S.n_heads, S.inter
+        p = lambda t: t.data_ptr()  # noqa: E731
+        h_a, h_b, xn = p(self.h_a), p(self.h_b), p(self.xn)
+        ws, wsb = p(self.gemm_ws), self.gemm_ws.numel()
+        first = self.rank == 0
+        chk(lib.qz_embed_gather(p(self.embed_q), p(self.embed_s), self.embed_s.shape[1],
+                                p(self.tok), B, S.vocab, H, h_a, st))
+        for li, L in enumerate(self.layers):
+            self._batch_layer_attn(li, L, st)
+            chk(lib.qz_gemm_w8_ws(p(L.o_q), p(L.o_s), L.o_s.shape[1], p(self.ao), h_b, B, H,
+                                  nq * hd, h_a if first else None, ws, wsb, st))
+            self._all_reduce(self.h_b[:B])
+            chk(lib.qz_rmsnorm(h_b, p(L.post_w), xn, B, H, S.eps, st))
+            chk(lib.qz_gemm_w8_ws(p(L.gu_q), p(L.gu_s), L.gu_s.shape[1], xn, p(self.gu), B,
+                                  2 * I, H, None, ws, wsb, st))
+            chk(lib.qz_silu_mul(p(self.gu), p(self.act), B, I, st))
+            chk(lib.qz_gemm_w8_ws(p(L.down_q), p(L.down_s), L.down_s.shape[1], p(self.act), h_a,
+                                  B, H, I, h_b if first else None, ws, wsb, st))
+            self._all_reduce(self.h_a[:B])
+        chk(lib.qz_rmsnorm(h_a, p(self.norm_w), xn, B, H, S.eps, st))
+        n_local = self.vhi - self.vlo
+        if n_local > 0:
+            chk(lib.qz_gemm_w8_ws(p(self.lm_q), p(self.lm_s), self.lm_s.shape[1], xn,
+                                  p(self.logits), B, n_local, H, None, ws, wsb, st))
+        self._pick_token(st, 1)
+
     def _decode_ops(self, st: int) -> None:
+        if self.batch > 1:
+            return self._decode_ops_batch(st)
         if self.fused_ar:
             return self._decode_ops_fused(st)
         S, lib, chk = self.spec, self.lib, _lib.check

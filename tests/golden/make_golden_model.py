@@ -15,6 +15,12 @@ is quantised with ``QuantConfig(default="int8", fused=True)``
 * ``kv``: fill every layer's KV cache with ``kv_len`` positions of N(0, 1)
   keys then values from ``default_rng(99)`` (layer by layer), then decode from
   token ``first``.
+* ``kv`` with ``batch`` B: B sequences decoded in lockstep through the
+  reference's batched path (decode_logits on [B, 1] ids, so every matmul has
+  M = B rows and the MLP takes quartz/quantize.py:112-114): the caches hold
+  [B, n_kv, kv_len, head_dim] draws per layer (keys then values, layer by
+  layer, from ``default_rng(99)``) and sequence b starts from ``firsts[b]``;
+  tokens are stored [steps, B].
 
 Stored per case (cases_model.json + golden_model.npz): the config, the greedy
 tokens, each step's top-1/top-2 logit margin, the top-8 (id, logit) of every
@@ -71,13 +77,28 @@ CASES = [
                   num_key_value_heads=8, head_dim=128, intermediate_size=3072,
                   vocab_size=151936, rope_theta=1000000.0, tie_word_embeddings=True),
          start="kv", kv_len=512, first=42, steps=128),
+    # batched decode (B sequences in lockstep, M = B rows per matmul)
+    dict(id="qwen3_small_kv_b3", arch="Qwen3ForCausalLM",
+         cfg=dict(hidden_size=256, num_hidden_layers=3, num_attention_heads=4,
+                  num_key_value_heads=2, head_dim=64, intermediate_size=512, vocab_size=1000,
+                  rope_theta=1000000.0, tie_word_embeddings=True),
+         start="kv", kv_len=100, batch=3, firsts=[3, 17, 500], steps=24),
+] + [
+    dict(id=f"qwen3_0p6b_kv512_b{B}", arch="Qwen3ForCausalLM",
+         cfg=dict(hidden_size=1024, num_hidden_layers=28, num_attention_heads=16,
+                  num_key_value_heads=8, head_dim=128, intermediate_size=3072,
+                  vocab_size=151936, rope_theta=1000000.0, tie_word_embeddings=True),
+         start="kv", kv_len=512, batch=B, firsts=[(42 + 9973 * b) % 151936 for b in range(B)],
+         steps=32)
+    for B in (2, 4, 8, 16)
+] + [
     # Llama-3.2-1B architecture: 512-token prefill, then greedy decoding
     dict(id="llama_1b_prompt512", arch="LlamaForCausalLM",
          cfg=dict(hidden_size=2048, num_hidden_layers=16, num_attention_heads=32,
                   num_key_value_heads=8, head_dim=64, intermediate_size=8192,
                   vocab_size=128256, rope_theta=500000.0, tie_word_embeddings=True,
                   rope_scaling=LLAMA3_SCALING),
-         start="prompt_rng", prompt_seed=7, prompt_len=512, steps=64),
+         start="prompt_rng", prompt_seed=7, prompt_len=512, steps=256),
 ]
 
 
@@ -119,14 +140,16 @@ def main(ref_root: str, only=None):
         quantize_model(net, QuantConfig(default="int8", fused=True))
         L = cfg.num_hidden_layers
         cache = make_cache(L)
+        B = case.get("batch", 1)
         if case["start"] == "kv":
             krng = np.random.default_rng(99)
-            shape = (1, cfg.num_key_value_heads, case["kv_len"], cfg.head_dim)
+            shape = (B, cfg.num_key_value_heads, case["kv_len"], cfg.head_dim)
             for c in cache:
                 k = krng.standard_normal(shape, dtype=np.float32)
                 v = krng.standard_normal(shape, dtype=np.float32)
                 c.update_and_fetch(k, v)
-            logits = net.decode_logits(np.array([[case["first"]]]), cache=cache)[:, -1, :]
+            firsts = case.get("firsts", [case.get("first")])
+            logits = net.decode_logits(np.array([[f] for f in firsts]), cache=cache)[:, -1, :]
         else:
             if case["start"] == "prompt_rng":
                 case["prompt"] = np.random.default_rng(case["prompt_seed"]).integers(
@@ -134,15 +157,18 @@ def main(ref_root: str, only=None):
             logits = net.decode_logits(np.array([case["prompt"]]), cache=cache)[:, -1, :]
         toks, margins, top_ids, top_vals = [], [], [], []
         for step in range(case["steps"]):
-            row = logits[0]
-            order = np.argsort(-row, kind="stable")[:8]
-            tok = int(np.argmax(row))
-            toks.append(tok)
-            margins.append(float(row[order[0]] - row[order[1]]))
-            top_ids.append(order)
-            top_vals.append(row[order])
+            row_toks = []
+            for b in range(B):
+                row = logits[b]
+                order = np.argsort(-row, kind="stable")[:8]
+                row_toks.append(int(np.argmax(row)))
+                margins.append(float(row[order[0]] - row[order[1]]))
+                top_ids.append(order)
+                top_vals.append(row[order])
+            toks.append(row_toks if B > 1 else row_toks[0])
             if step + 1 < case["steps"]:
-                logits = net.decode_logits(np.array([[tok]]), cache=cache)[:, -1, :]
+                logits = net.decode_logits(np.array([[t] for t in row_toks]),
+                                           cache=cache)[:, -1, :]
         emb = net.model.embed_tokens
         l0 = net.model.layers[0]
         digests = dict(embed_q=_digest(emb.q), embed_s=_digest(emb.scale),

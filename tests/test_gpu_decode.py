@@ -225,10 +225,10 @@ def _golden(cid, key):
 
 def _engine(case, extra_ctx=0, persistent=False, fold_norms=True):
     from quartz_b200.decode import DecodeEngine
-    from quartz_b200.model import ModelSpec, norm_weights, random_int8_weights
+    from quartz_b200.model import ModelSpec, cached_int8_weights, norm_weights
     spec = ModelSpec.from_hf(case["cfg"], case["arch"])
     start = case.get("kv_len") or len(case["prompt"])
-    eng = DecodeEngine(spec, random_int8_weights(spec), norm_weights(spec),
+    eng = DecodeEngine(spec, cached_int8_weights(spec), norm_weights(spec),
                        max_ctx=start + case["steps"] + extra_ctx,
                        max_prefill=max(2, len(case.get("prompt", [])) or 2),
                        persistent=persistent, fold_norms=fold_norms)

@@ -94,6 +94,59 @@ def test_tp_decode_tokens_match_reference(world):
     mp.spawn(_worker, args=(world, _free_port(), cids, variants), nprocs=world, join=True)
 
 
+def _batch_worker(rank, world, port, cids, variants):
+    import sys
+    sys.path.insert(0, REPO)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    torch.distributed.init_process_group(
+        "nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+        timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+    from quartz_b200 import device
+    from quartz_b200.model import ModelSpec, cached_int8_weights, norm_weights, seeded_kv
+    from quartz_b200.tp_decode import TPDecodeEngine
+    cases = {c["id"]: c for c in json.loads((GOLD / "cases_model.json").read_text())["cases"]}
+    try:
+        with np.load(GOLD / "golden_model.npz") as z:
+            golds = {cid: z[f"{cid}__tokens"].tolist() for cid in cids}
+        for cid in cids:
+            case = cases[cid]
+            spec = ModelSpec.from_hf(case["cfg"], case["arch"])
+            B = case["batch"]
+            for allreduce, graph in variants:
+                eng = TPDecodeEngine(spec, cached_int8_weights(spec), norm_weights(spec),
+                                     max_ctx=case["kv_len"] + case["steps"], max_prefill=1,
+                                     device=torch.device("cuda", rank), allreduce=allreduce,
+                                     batch=B)
+                eng.load_kv(seeded_kv(spec, case["kv_len"], batch=B))
+                toks = eng.generate_batch(case["firsts"], case["steps"], graph=graph, unroll=8)
+                assert toks == golds[cid], (cid, allreduce, graph, rank)
+                eng.close()
+                del eng
+                torch.cuda.synchronize()
+        device.check_status(torch.device("cuda", rank))
+    finally:
+        torch.distributed.destroy_process_group()
+
+
+TP_BATCH_CASES = {
+    2: (["qwen3_0p6b_kv512_b4"], (("nccl", False), ("peer", True), ("fused", True))),
+    4: (["qwen3_0p6b_kv512_b8"], (("peer", True),)),
+    8: (["qwen3_0p6b_kv512_b16", "qwen3_0p6b_kv512_b2"], (("nccl", True), ("peer", True))),
+}
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_batch_decode_tokens_match_reference(world):
+    """B sequences in lockstep over the ranks ([B, H] all-reduces): every row's
+    greedy tokens equal quartz's batched decode."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    cids, variants = TP_BATCH_CASES[world]
+    mp.spawn(_batch_worker, args=(world, _free_port(), cids, variants), nprocs=world, join=True)
+
+
 def _ar_worker(rank, world, port):
     import sys
     sys.path.insert(0, REPO)
