@@ -178,10 +178,10 @@ def cached_int8_weights(spec: ModelSpec, seed: int = 1234, std: float = 0.02,
     shapes = leaf_names(spec)
 
     def load():
-        # two flat files (all q bytes, all scales) mapped read-only; the
+        # two flat files (all q bytes, all scales) mapped copy-on-write; the
         # tensors are views into them, in leaf order
-        qb = np.load(base + "_q.npy", mmap_mode="r")
-        sb = np.load(base + "_s.npy", mmap_mode="r")
+        qb = np.load(base + "_q.npy", mmap_mode="c")
+        sb = np.load(base + "_s.npy", mmap_mode="c")
         out, oq, os_ = [], 0, 0
         for name, (n, k) in shapes:
             if oq + n * k > qb.size or os_ + n > sb.size:
