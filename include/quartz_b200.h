@@ -224,7 +224,14 @@ int qz_qk_rope(const float* qkv, const float* q_norm_w, const float* k_norm_w,
 /* Workspace bytes the decode attention entry points need for contexts up to
  * max_ctx on the current device. The workspace must be 256-byte aligned and
  * zeroed once before its first use (the kernels leave it ready for the next
- * call); calls sharing one workspace must not overlap on the GPU. */
+ * call); calls sharing one workspace must not overlap on the GPU.
+ *
+ * The decode attention kernels launch as programmatic dependents of the
+ * previous kernel in the stream and start copying cache rows 0 .. T-2 before
+ * they wait for it (row T-1, the newest, only after): those rows must have
+ * been written by work that completed before the previous kernel started --
+ * host copies, or kernels with an ordinary (non-programmatic) launch after
+ * them, like the per-token embedding gather and argmax of a decode loop. */
 int qz_attention_decode_workspace_bytes(int nq, int nkv, int hd, int64_t max_ctx, int64_t* bytes);
 
 /*

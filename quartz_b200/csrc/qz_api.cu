@@ -56,18 +56,22 @@ cudaError_t allow_smem(F* fn, int bytes) {
   return cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
-template <int R>
+template <int R, int D = qz::kDepth>
 cudaError_t allow_gemv_variants(int smem) {
   cudaError_t e = cudaSuccess;
   auto set = [&](auto fn) { if (e == cudaSuccess) e = allow_smem(fn, smem); };
-  set(qz::gemv_kernel<R, true, qz::K1K, kMinBlocks>);
-  set(qz::gemv_kernel<R, true, qz::KFULL, kMinBlocks>);
-  set(qz::gemv_kernel<R, true, qz::KANY, kMinBlocks>);
-  set(qz::gemv_kernel<R, false, qz::K1K, kMinBlocks>);
-  set(qz::gemv_kernel<R, false, qz::KFULL, kMinBlocks>);
-  set(qz::gemv_kernel<R, false, qz::KANY, kMinBlocks>);
+  set(qz::gemv_kernel<R, true, qz::K1K, kMinBlocks, D>);
+  set(qz::gemv_kernel<R, true, qz::KFULL, kMinBlocks, D>);
+  set(qz::gemv_kernel<R, true, qz::KANY, kMinBlocks, D>);
+  set(qz::gemv_kernel<R, false, qz::K1K, kMinBlocks, D>);
+  set(qz::gemv_kernel<R, false, qz::KFULL, kMinBlocks, D>);
+  set(qz::gemv_kernel<R, false, qz::KANY, kMinBlocks, D>);
   return e;
 }
+
+// Ring depth of one-row GEMV walks when three CTAs per SM still fit: 6 KB in
+// flight per warp instead of 2.
+constexpr int kDeepRing = 6;
 
 template <int R, bool ANY>
 cudaError_t allow_gemv_w4_variants(int smem) {
@@ -120,6 +124,7 @@ int device_info(DeviceInfo** out) {
       const int smem = d.smem_optin - 256;
       QZ_CUDA(allow_gemv_variants<kTallRows>(smem));
       QZ_CUDA(allow_gemv_variants<1>(smem));
+      QZ_CUDA((allow_gemv_variants<1, kDeepRing>(smem)));
       QZ_CUDA((allow_gemv_w4_variants<2 * kTallRows, false>(smem)));
       QZ_CUDA((allow_gemv_w4_variants<2, true>(smem)));
       QZ_CUDA(allow_mlp_variants<kTallRows>(smem));
@@ -207,10 +212,11 @@ int blocks_per_sm(F* fn, int smem, int* out) {
   return QZ_OK;
 }
 
-template <int R, bool PER_ROW, int KM>
+template <int R, bool PER_ROW, int KM, int D = qz::kDepth>
 int launch_gemv(const DeviceInfo& d, const qz::GemvArgs& a, cudaStream_t st) {
-  auto fn = qz::gemv_kernel<R, PER_ROW, KM, kMinBlocks>;
-  const int smem = KM == qz::K1K ? qz::ring_bytes(R) : qz::stream_smem_bytes(R, a.K);
+  auto fn = qz::gemv_kernel<R, PER_ROW, KM, kMinBlocks, D>;
+  const int ring = qz::kWarps * D * R * qz::kSegBytes;
+  const int smem = (KM == qz::K1K ? 0 : qz::stream_x_bytes(a.K)) + ring;
   int nb = 0;
   if (int rc = blocks_per_sm(fn, smem, &nb)) return rc;
   if (nb < 1) return fail(QZ_ERR_UNSUPPORTED, "gemv: shared memory does not fit");
@@ -221,6 +227,21 @@ int launch_gemv(const DeviceInfo& d, const qz::GemvArgs& a, cudaStream_t st) {
 
 template <int R, bool PER_ROW>
 int launch_gemv_k(const DeviceInfo& d, const qz::GemvArgs& a, cudaStream_t st) {
+  if constexpr (R == 1) {
+    // one-row groups: the deep ring when x plus the ring leave room for three
+    // CTAs on an SM
+    const int x = kmode(a.K) == qz::K1K && !a.norm_w ? 0 : qz::stream_x_bytes(a.K);
+    const int deep = x + qz::kWarps * kDeepRing * qz::kSegBytes;
+    if (deep * kMinBlocks <= d.smem_optin - 256 * kMinBlocks) {
+      switch (kmode(a.K)) {
+        case qz::K1K:
+          if (a.norm_w) return launch_gemv<1, PER_ROW, qz::KFULL, kDeepRing>(d, a, st);
+          return launch_gemv<1, PER_ROW, qz::K1K, kDeepRing>(d, a, st);
+        case qz::KFULL: return launch_gemv<1, PER_ROW, qz::KFULL, kDeepRing>(d, a, st);
+        default: return launch_gemv<1, PER_ROW, qz::KANY, kDeepRing>(d, a, st);
+      }
+    }
+  }
   switch (kmode(a.K)) {
     case qz::K1K:
       // A folded RMSNorm needs x staged in shared memory (one coalesced pass
@@ -912,7 +933,18 @@ AttnLayout attn_layout(const DeviceInfo& d, int nq, int nkv, int hd, int64_t max
 template <int E, int NR, bool QKV>
 int launch_attn_fused(const qz::dec::AttnArgs& a, int S, cudaStream_t st, int batch = 1) {
   constexpr int smem = qz::dec::attn_fused_smem<E, NR>();
-  static_assert(smem <= 48 * 1024, "fused attention shared memory above the default limit");
+  static_assert(smem <= 200 * 1024, "fused attention shared memory above the opt-in limit");
+  // above 48 KB the launch needs the opt-in limit, set once per device
+  static std::once_flag once[kMaxDevices];
+  int dev = 0;
+  QZ_CUDA(cudaGetDevice(&dev));
+  if (dev < 0 || dev >= kMaxDevices) return fail(QZ_ERR_UNSUPPORTED, "device index out of range");
+  cudaError_t ae = cudaSuccess;
+  std::call_once(once[dev], [&] {
+    ae = cudaFuncSetAttribute(qz::dec::attn_decode_fused_kernel<E, NR, QKV>,
+                              cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  });
+  QZ_CUDA(ae);
   // a programmatic dependent launch: the kernel hints its cache rows into L2
   // before griddepcontrol.wait and lets the next kernel launch early
   cudaLaunchConfig_t cfg = {};

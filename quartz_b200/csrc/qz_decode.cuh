@@ -596,13 +596,33 @@ __device__ __forceinline__ void norm_rope(float (&x)[E], const float* __restrict
   }
 }
 
+// Positions per warp per round of the fused attention: a round's K and V rows
+// are one cp.async group in the warp's private two-round ring.
+template <int E>
+__host__ __device__ constexpr int attn_round() { return E >= 8 ? 2 : 4; }
+
+// Copy this lane's E floats of cache row `src` to shared memory `dst` (its own
+// bytes of the warp's ring slot; the lane later reads back exactly these).
+template <int E>
+__device__ __forceinline__ void cp_async_lane(uint32_t dst, const float* src) {
+  if constexpr (E % 4 == 0) {
+#pragma unroll
+    for (int e = 0; e < E; e += 4) cp_async16(dst + 4 * e, src + e);
+  } else {
+    static_assert(E == 2, "lane slices of 2, 4 or 8 floats");
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+  }
+}
+
 template <int E, int NR, bool QKV>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_fused_kernel(AttnArgs a) {
   constexpr int HD = 32 * E;
-  constexpr int U = E >= 8 ? 2 : 4;   // positions per warp per round
+  constexpr int U = attn_round<E>();   // positions per warp per round
   extern __shared__ float4 attn_smem4[];
   float* qs = reinterpret_cast<float*>(attn_smem4);   // [NR][HD]
   float* red = qs + NR * HD;                           // [warps][NR][HD + 2]
+  // per warp: 2 rounds x U positions x (K row, V row)
+  float* ring = red + kAttnWarps * NR * (HD + 2);
   __shared__ unsigned s_last;
   const int g = blockIdx.x, c = blockIdx.y, S = gridDim.y;
   const int64_t b = blockIdx.z;
@@ -611,31 +631,54 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_fused_kernel(AttnArg
   float* const kc = a.kc + b * a.kv_bstride;
   float* const vc = a.vc + b * a.kv_bstride;
   const int64_t kv_off = static_cast<int64_t>(g) * a.max_ctx * HD;
-  // Launched as a programmatic dependent of the projection that writes `in`:
-  // the next kernel may launch now (it waits for this grid's completion),
-  // and before waiting for the previous grid this CTA only hints the cache
-  // rows it will read into L2. The context length read here can be stale;
-  // the rows are clamped inside the cache, and everything after the wait
-  // reads it again.
-  pdl_trigger();
-  {
-    int64_t Tp = (a.len_dev ? *a.len_dev : a.len0) + a.len_off;
-    Tp = Tp > a.max_ctx ? a.max_ctx : (Tp < 0 ? 0 : Tp);
-    const int64_t per_p = Tp > 0 ? (cdiv(Tp, S) + 7) / 8 * 8 : 0;
-    const int64_t p0 = static_cast<int64_t>(c) * per_p, p1 = min64(Tp, p0 + per_p);
-    constexpr int kLines = HD * 4 / 128;   // 128-byte lines per cache row
-    for (int64_t i = threadIdx.x; i < (p1 - p0) * 2 * kLines; i += kAttnThreads) {
-      const int64_t t = p0 + i / (2 * kLines);
-      const int j = static_cast<int>(i % (2 * kLines));
-      prefetch_l2((j < kLines ? kc : vc) + kv_off + t * HD + (j % kLines) * 32);
+  float* const wring = ring + warp * (2 * U * 2 * HD);
+  const uint32_t wring_s = smem_u32(wring);
+
+  // This CTA's positions [t0, t1) for context length T; warp w takes positions
+  // t0 + w + 8 i, i = 0, 1, ..., U of them per round.
+  auto range = [&](int64_t T, int64_t& t0, int64_t& t1) {
+    const int64_t per = T > 0 ? (cdiv(T, S) + 7) / 8 * 8 : 0;
+    t0 = static_cast<int64_t>(c) * per;
+    t1 = min64(T, t0 + per);
+  };
+  auto ctx = [&]() {
+    int64_t T = (a.len_dev ? *a.len_dev : a.len0) + a.len_off;
+    return T > a.max_ctx ? a.max_ctx : (T < 0 ? 0 : T);
+  };
+  // Issue round r's rows among positions [lo, hi), one commit group per call.
+  auto issue_round = [&](int64_t r, int64_t t0, int64_t lo, int64_t hi) {
+    const uint32_t slot = wring_s + static_cast<uint32_t>((r & 1) * U * 2 * HD * 4);
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t t = t0 + warp + static_cast<int64_t>(kAttnWarps) * (r * U + u);
+      if (t >= lo && t < hi) {
+        const uint32_t d = slot + static_cast<uint32_t>(u * 2 * HD * 4 + lane * E * 4);
+        cp_async_lane<E>(d, kc + kv_off + t * HD + lane * E);
+        cp_async_lane<E>(d + HD * 4, vc + kv_off + t * HD + lane * E);
+      }
     }
-  }
+    cp_async_commit();
+  };
+
+  // Launched as a programmatic dependent of the kernel that writes `in` (and,
+  // without QKV, the newest cache row): the next kernel may launch now. Rows
+  // before the newest one were written by earlier steps, so the first two
+  // rounds of them go in flight before the wait, for the context length read
+  // here; after the wait the length is read again and, if it moved, the ring
+  // is drained and refilled.
+  pdl_trigger();
+  const int64_t T_pre = ctx();
+  int64_t t0, t1;
+  range(T_pre, t0, t1);
+  issue_round(0, t0, t0, min64(t1, T_pre - 1));
+  issue_round(1, t0, t0, min64(t1, T_pre - 1));
   pdl_wait();
-  int64_t T = (a.len_dev ? *a.len_dev : a.len0) + a.len_off;
-  T = T > a.max_ctx ? a.max_ctx : T;
-  const int64_t per = T > 0 ? (cdiv(T, S) + 7) / 8 * 8 : 0;
-  const int64_t t0 = static_cast<int64_t>(c) * per;
-  const int64_t t1 = min64(T, t0 + per);
+  const int64_t T = ctx();
+  const bool moved = T != T_pre;
+  if (moved) {
+    cp_async_wait<0>();
+    range(T, t0, t1);
+  }
   const int64_t pos = T - 1;
   // the append happens only for a position inside the cache
   const int64_t t_raw = (a.len_dev ? *a.len_dev : a.len0) + a.len_off;
@@ -664,6 +707,28 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_fused_kernel(AttnArg
       }
     }
     __syncthreads();   // queries in shared memory; the appended row visible to the CTA
+    if (moved) {
+      issue_round(0, t0, t0, t1);
+      issue_round(1, t0, t0, t1);
+    } else if (T_pre - 1 < t1) {
+      // the newest row (and anything after it in this CTA's range) of the
+      // first two rounds, now that it is written; then let everything land
+      const int64_t lo = T_pre - 1 > t0 ? T_pre - 1 : t0;
+      for (int64_t r = 0; r < 2; ++r) {
+        const uint32_t slot = wring_s + static_cast<uint32_t>((r & 1) * U * 2 * HD * 4);
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+          const int64_t t = t0 + warp + static_cast<int64_t>(kAttnWarps) * (r * U + u);
+          if (t >= lo && t < t1) {
+            const uint32_t d = slot + static_cast<uint32_t>(u * 2 * HD * 4 + lane * E * 4);
+            cp_async_lane<E>(d, kc + kv_off + t * HD + lane * E);
+            cp_async_lane<E>(d + HD * 4, vc + kv_off + t * HD + lane * E);
+          }
+        }
+      }
+      cp_async_commit();
+      cp_async_wait<0>();
+    }
 
     float q[NR][E], acc[NR][E], m[NR], l[NR];
 #pragma unroll
@@ -676,16 +741,24 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_fused_kernel(AttnArg
         acc[r][e] = 0.f;
       }
     }
-    for (int64_t tb = t0 + warp; tb < t1; tb += kAttnWarps * U) {
+    const int64_t n_w = t1 - t0 > warp ? (t1 - t0 - warp + kAttnWarps - 1) / kAttnWarps : 0;
+    const int64_t rounds = (n_w + U - 1) / U;
+    for (int64_t rd = 0; rd < rounds; ++rd) {
+      // rounds rd and rd + 1 were issued before; issue rd + 1 into the slot
+      // round rd - 1 vacated, then round rd has landed once at most one group
+      // is pending
+      if (rd >= 1) issue_round(rd + 1, t0, t0, t1);
+      cp_async_wait<1>();
+      const float* slot = wring + (rd & 1) * U * 2 * HD;
       float kr[U][E], vr[U][E];
       bool ok[U];
 #pragma unroll
       for (int u = 0; u < U; ++u) {
-        const int64_t t = tb + u * kAttnWarps;
+        const int64_t t = t0 + warp + static_cast<int64_t>(kAttnWarps) * (rd * U + u);
         ok[u] = t < t1;
         if (ok[u]) {
-          load_vec<E>(kc + kv_off + t * HD + lane * E, kr[u]);
-          load_vec<E>(vc + kv_off + t * HD + lane * E, vr[u]);
+          load_vec<E>(slot + u * 2 * HD + lane * E, kr[u]);
+          load_vec<E>(slot + u * 2 * HD + HD + lane * E, vr[u]);
         } else {
 #pragma unroll
           for (int e = 0; e < E; ++e) kr[u][e] = vr[u][e] = 0.f;
@@ -726,6 +799,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_fused_kernel(AttnArg
         m[r] = mx;
       }
     }
+    cp_async_wait<0>();
     // merge the warps: per-warp (acc, m, l) to shared memory, then one partial per head
 #pragma unroll
     for (int r = 0; r < NR; ++r) {
@@ -753,6 +827,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_fused_kernel(AttnArg
       if (d == 0) { pbase[r * (HD + 2) + HD] = M; pbase[r * (HD + 2) + HD + 1] = den; }
     }
   } else {
+    cp_async_wait<0>();
     for (int r = threadIdx.x; r < NR; r += kAttnThreads) {
       pbase[r * (HD + 2) + HD] = -INFINITY;
       pbase[r * (HD + 2) + HD + 1] = 0.f;
@@ -777,7 +852,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_fused_kernel(AttnArg
 
 template <int E, int NR>
 constexpr int attn_fused_smem() {
-  return (NR * 32 * E + kAttnWarps * NR * (32 * E + 2)) * 4;
+  return (NR * 32 * E + kAttnWarps * NR * (32 * E + 2) + kAttnWarps * 2 * attn_round<E>() * 2 * 32 * E) * 4;
 }
 
 // Greedy argmax of each row of logits [M, V]: a block reduces a slice of a row

@@ -94,14 +94,6 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
 }
-// Wait until the grids this one depends on have completed and their memory is
-// visible (a no-op without a programmatic dependency).
-__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-// Allow the next kernel in the stream to begin launching; it still waits for
-// this grid's completion before it reads anything this grid writes.
-__device__ __forceinline__ void pdl_trigger() {
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
-}
 
 // Stage K activations into shared memory as float4 blocks ordered [word j4][chunk c].
 // COHERENT: the source was written earlier in this kernel by other CTAs (the
@@ -397,28 +389,30 @@ __device__ __forceinline__ void split_range(int64_t n, int64_t parts, int64_t p,
 // ---------------------------------------------------------------------------
 // GEMV
 // ---------------------------------------------------------------------------
-template <int R, bool PER_ROW, int KM, int MINB>
+// D: items in a warp's ring. Four-row groups use kDepth; one-row groups (few
+// rows per warp) a deeper ring of 1 KB items, so that a warp keeps as many
+// bytes in flight as a four-row walk does.
+template <int R, bool PER_ROW, int KM, int MINB, int D = kDepth>
 __global__ void __launch_bounds__(kThreads, MINB) gemv_kernel(const GemvArgs a) {
   extern __shared__ __align__(128) uint8_t smem[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   float* xs = reinterpret_cast<float*>(smem);
   const uint8_t* ring =
-      smem + (KM == K1K ? 0 : stream_x_bytes(a.K)) + warp * kDepth * R * kSegBytes;
+      smem + (KM == K1K ? 0 : stream_x_bytes(a.K)) + warp * D * R * kSegBytes;
   const uint32_t ring_s = smem_u32(ring);
 
   const int64_t nw = static_cast<int64_t>(gridDim.x) * kWarps;
   const int64_t wg = static_cast<int64_t>(blockIdx.x) * kWarps + warp;
   int64_t r0, r1;
   split_range(a.N, nw, wg, r0, r1);
-  const Walk<R> w{a.q, a.K, cdiv(r1 - r0, R), static_cast<int>(cdiv(a.K, kSegBytes)), 0};
+  const Walk<R, D> w{a.q, a.K, cdiv(r1 - r0, R), static_cast<int>(cdiv(a.K, kSegBytes)), 0};
   auto rowfn = [&](int64_t g, int r) -> int64_t {
     const int64_t row = r0 + g * R + r;
     return row < r1 ? row : -1;
   };
   // The weights do not depend on the previous grid: fill the whole ring
   // before waiting for it.
-  issue_item<R, KM>(w, ring_s, cursor_at(w, 0), lane, rowfn);
-  issue_item<R, KM>(w, ring_s, cursor_at(w, kDepth - 1), lane, rowfn);
+  issue_items<R, KM>(w, ring_s, 0, D, lane, rowfn);
   if constexpr (KM != K1K) {
     if (a.norm_w)
       for (int64_t i = tid * 32; i < a.K; i += kThreads * 32) prefetch_l1(a.norm_w + i);

@@ -107,7 +107,18 @@ def mlp_algorithmic_bytes(H, I, ng=1, ngd=1, M=1) -> int:
 #                                                   positions, T eager tokens
 #   python -m quartz_b200.workloads decode8b [--tokens T]
 #                                                   Qwen3-8B shapes, context 2048
+#   python -m quartz_b200.workloads batch8b --batch B [--tokens T]
+#                                                   Qwen3-8B shapes, B sequences
+#                                                   in lockstep, context 2048
+#   python -m quartz_b200.workloads mlp8b           one Qwen3-8B fused MLP layer
+#                                                   (H 4096, I 12288), 3 calls
+#   python -m quartz_b200.workloads attn8b          decode attention, Qwen3-8B
+#                                                   heads, context 2048, 3 calls
 #   python -m quartz_b200.workloads prefill         Llama-3.2-1B 512-token prefill
+#
+# --profile-last (decode, decode8b, batch8b, mlp8b, attn8b): the last token /
+# call runs between cudaProfilerStart and cudaProfilerStop, for a profiler run
+# with --profile-from-start off.
 # ---------------------------------------------------------------------------
 def _main(argv=None) -> None:
     import argparse
@@ -127,11 +138,30 @@ def _main(argv=None) -> None:
     d.add_argument("--tokens", type=int, default=3)
     d8 = sub.add_parser("decode8b")
     d8.add_argument("--tokens", type=int, default=3)
+    b8 = sub.add_parser("batch8b")
+    b8.add_argument("--batch", type=int, default=16)
+    b8.add_argument("--tokens", type=int, default=3)
+    sub.add_parser("mlp8b")
+    sub.add_parser("attn8b")
     sub.add_parser("prefill")
-    a = ap.parse_args(argv)
+    for p_ in (d, d8, b8):
+        p_.add_argument("--profile-last", action="store_true")
+    a, rest = ap.parse_known_args(argv)
+    a.profile_last = getattr(a, "profile_last", False) or "--profile-last" in rest
     dev = torch.device("cuda", 0)
     from . import device as qd
     qd.ensure_device(dev)
+
+    def profiled(fn):
+        """Run fn once more, inside the profiler range when asked."""
+        torch.cuda.synchronize()
+        if a.profile_last:
+            torch.cuda.profiler.start()
+        r = fn()
+        torch.cuda.synchronize()
+        if a.profile_last:
+            torch.cuda.profiler.stop()
+        return r
     if a.what == "gemm":
         c = gemv_case(a.N, a.K, M=a.M, seed=0)
         q, s = torch.from_numpy(c.q).to(dev), torch.from_numpy(c.scale).to(dev)
@@ -154,6 +184,36 @@ def _main(argv=None) -> None:
             y4 = qd.gemv_w4(q4d, s4d, x)
         torch.cuda.synchronize()
         print(f"lm4: |y8|max {float(y8.abs().max()):.4g}, |y4|max {float(y4.abs().max()):.4g}")
+    elif a.what == "mlp8b":
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(5)
+        H, I = 4096, 12288
+        gq = torch.randint(-127, 128, (2 * I, H), dtype=torch.int8, device=dev, generator=gen)
+        dq = torch.randint(-127, 128, (H, I), dtype=torch.int8, device=dev, generator=gen)
+        gs = torch.rand(2 * I, 1, device=dev, generator=gen) * 1e-3
+        ds = torch.rand(H, 1, device=dev, generator=gen) * 1e-3
+        x = torch.randn(H, device=dev, generator=gen)
+        for _ in range(2):
+            out = qd.fused_mlp(gq, gs, x, dq, ds)
+        out = profiled(lambda: qd.fused_mlp(gq, gs, x, dq, ds))
+        print(f"mlp8b: |out|max {float(out.abs().max()):.4g}")
+    elif a.what == "attn8b":
+        from .model import QWEN3_8B, rope_inv_freq
+        S8 = QWEN3_8B
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(6)
+        kc = torch.randn(S8.n_kv, 2112, S8.head_dim, device=dev, generator=gen)
+        vc = torch.randn(S8.n_kv, 2112, S8.head_dim, device=dev, generator=gen)
+        qkv = torch.randn(S8.qkv_rows, device=dev, generator=gen)
+        inv = torch.from_numpy(rope_inv_freq(S8)).to(dev)
+        qn = torch.ones(S8.head_dim, device=dev)
+        pos = torch.tensor([2048], dtype=torch.int64, device=dev)
+        for _ in range(2):
+            o = qd.attention_decode_qkv(qkv, inv, kc, vc, S8.n_heads, pos_dev=pos, q_norm=qn,
+                                        k_norm=qn)
+        o = profiled(lambda: qd.attention_decode_qkv(qkv, inv, kc, vc, S8.n_heads, pos_dev=pos,
+                                                     q_norm=qn, k_norm=qn))
+        print(f"attn8b: |out|max {float(o.abs().max()):.4g}")
     elif a.what == "mlp":
         for l in range(MLP_LAYERS):
             m = mlp_case(MLP_H, MLP_I, seed=MLP_LAYER_SEED0 + l)
@@ -169,19 +229,35 @@ def _main(argv=None) -> None:
             eng = DecodeEngine(spec, random_int8_weights(spec), norm_weights(spec), max_ctx=640,
                                max_prefill=1, device=dev, persistent=a.persistent)
             eng.load_kv(seeded_kv(spec, 512))
-            toks = eng.generate(42, a.tokens, graph=False)
+            toks = eng.generate(42, a.tokens - 1, graph=False)
+            toks.append(profiled(lambda: eng.decode(toks[-1])))
             print(f"decode ({'persistent' if eng.persistent else 'per-op'}): {toks}")
-        elif a.what == "decode8b":
-            # Qwen3-8B shapes on one GPU, device-drawn weights, context 2048
+        elif a.what in ("decode8b", "batch8b"):
+            # Qwen3-8B shapes on one GPU, device-drawn weights and caches, context 2048
             from .model import QWEN3_8B
             from .tp_decode import random_tp_shard
+            B = a.batch if a.what == "batch8b" else 1
             local, w, (lq, ls, _, _) = random_tp_shard(QWEN3_8B, 0, 1, dev)
             eng = DecodeEngine(local, w, norm_weights(QWEN3_8B), max_ctx=2048 + a.tokens,
-                               max_prefill=1, device=dev)
+                               max_prefill=1, device=dev, batch=B)
+            del w
             eng.lm_q, eng.lm_s = lq, ls
+            eng.k_cache.normal_()
+            eng.v_cache.normal_()
             eng.reset(2048)
-            toks = eng.generate(7, a.tokens, graph=False)
-            print(f"decode8b: {toks}")
+            if B == 1:
+                toks = eng.generate(7, a.tokens - 1, graph=False)
+                toks.append(profiled(lambda: eng.decode(toks[-1])))
+            else:
+                firsts = [(7 + 7919 * b) % QWEN3_8B.vocab for b in range(B)]
+                toks = eng.generate_batch(firsts, a.tokens - 1, graph=False)
+
+                def last_step():
+                    eng._decode_ops_batch(eng._stream())
+                    eng.pos += 1
+                    return eng.tok.tolist()
+                toks.append(profiled(last_step))
+            print(f"{a.what}: {toks[-1]}")
         else:
             spec = LLAMA_3P2_1B
             eng = DecodeEngine(spec, random_int8_weights(spec), norm_weights(spec), max_ctx=600,
