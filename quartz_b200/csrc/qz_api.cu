@@ -445,8 +445,8 @@ int tc_gemm(const DeviceInfo& d, const int8_t* q, const float* scale, const floa
                      ? reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + L.limb_bytes +
                                                   L.sx_bytes)
                      : nullptr;
-  qz::tc::split_x_kernel<<<static_cast<unsigned>(L.mpad), 256, 0, st>>>(X, limbs, sx, M, L.mpad,
-                                                                          K);
+  qz::tc::split_x_kernel<<<static_cast<unsigned>(L.mpad), qz::tc::kSplitThreads, 0, st>>>(
+      X, limbs, sx, M, L.mpad, K);
   QZ_CUDA(cudaGetLastError());
   CUtensorMap tq, tx;
   if (int rc = make_tmap_u8(&tq, q, N, K, qz::tc::kRows)) return rc;
@@ -910,11 +910,15 @@ struct AttnLayout {
 
 // Context splits per kv head: about one CTA per SM in all (more splits cost
 // more in the merge than they gain: 19 vs 24 us at Qwen3-8B shapes, context
-// 2048), at least 32 positions per split, at most 256 (the merge's shared
-// scratch holds 2 n_rep S + n_rep floats).
+// 2048), at least 32 positions per split, at most 32: the last CTA of a kv
+// head merges the splits' partials in rounds of dependent L2 loads, so a
+// tensor-parallel rank with one or two kv heads would otherwise spend more
+// on the merge (66 splits at one kv head and context 2112) than on its
+// share of the cache.
+constexpr int kMaxAttnSplits = 32;
 int attn_splits(const DeviceInfo& d, int nkv, int64_t max_ctx) {
   const int64_t s = std::min<int64_t>(std::min<int64_t>(qz::cdiv(d.sms, nkv),
-                                                         qz::cdiv(max_ctx, 32)), 256);
+                                                         qz::cdiv(max_ctx, 32)), kMaxAttnSplits);
   return static_cast<int>(std::max<int64_t>(1, s));
 }
 

@@ -59,10 +59,28 @@ struct TcArgs {
 // ---------------------------------------------------------------------------
 // activation split: one CTA per (padded) activation row
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) split_x_kernel(const float* __restrict__ X,
-                                                      int8_t* __restrict__ limbs,
-                                                      float* __restrict__ sx, int64_t M,
-                                                      int64_t Mpad, int64_t K) {
+constexpr int kSplitThreads = 512;
+
+// One value's three limbs: v = d2 * 2^16 + d1 * 2^8 + d0, each in [-128, 127].
+__device__ __forceinline__ void limbs3(float x, float inv, int& d0, int& d1, int& d2) {
+  const int v = __float2int_rn(x * inv);
+  d0 = ((v + 128) & 255) - 128;
+  const int v1 = (v - d0) >> 8;
+  d1 = ((v1 + 128) & 255) - 128;
+  d2 = (v1 - d1) >> 8;
+}
+
+__device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
+  return (static_cast<uint32_t>(a) & 255u) | ((static_cast<uint32_t>(b) & 255u) << 8) |
+         ((static_cast<uint32_t>(c) & 255u) << 16) | ((static_cast<uint32_t>(d) & 255u) << 24);
+}
+
+// K % 4 == 0 and 16-byte aligned rows: float4 loads, one 4-byte store per
+// limb per 4 activations; otherwise element by element.
+__global__ void __launch_bounds__(kSplitThreads) split_x_kernel(const float* __restrict__ X,
+                                                                int8_t* __restrict__ limbs,
+                                                                float* __restrict__ sx, int64_t M,
+                                                                int64_t Mpad, int64_t K) {
   const int64_t m = blockIdx.x;
   int8_t* l0 = limbs + m * K;
   int8_t* l1 = limbs + (Mpad + m) * K;
@@ -73,9 +91,17 @@ __global__ void __launch_bounds__(256) split_x_kernel(const float* __restrict__ 
     return;
   }
   const float* xr = X + m * K;
+  const bool vec = (K & 3) == 0 && (reinterpret_cast<uintptr_t>(xr) & 15u) == 0;
   float mx = 0.f;
-  for (int64_t k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(xr[k]));
-  __shared__ float red[8];
+  if (vec) {
+    for (int64_t k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
+      const float4 v = *reinterpret_cast<const float4*>(xr + k);
+      mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+  } else {
+    for (int64_t k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(xr[k]));
+  }
+  __shared__ float red[kSplitThreads / 32];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
@@ -84,15 +110,26 @@ __global__ void __launch_bounds__(256) split_x_kernel(const float* __restrict__ 
   for (int w = 1; w < static_cast<int>(blockDim.x >> 5); ++w) mx = fmaxf(mx, red[w]);
   const float s = mx > 0.f ? mx / kLimbRange : 1.0f;
   const float inv = 1.0f / s;
-  for (int64_t k = threadIdx.x; k < K; k += blockDim.x) {
-    const int v = __float2int_rn(xr[k] * inv);
-    const int d0 = ((v + 128) & 255) - 128;
-    const int v1 = (v - d0) >> 8;
-    const int d1 = ((v1 + 128) & 255) - 128;
-    const int d2 = (v1 - d1) >> 8;
-    l0[k] = static_cast<int8_t>(d0);
-    l1[k] = static_cast<int8_t>(d1);
-    l2[k] = static_cast<int8_t>(d2);
+  if (vec) {
+    for (int64_t k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
+      const float4 v = *reinterpret_cast<const float4*>(xr + k);
+      int a0, a1, a2, b0, b1, b2, c0, c1, c2, e0, e1, e2;
+      limbs3(v.x, inv, a0, a1, a2);
+      limbs3(v.y, inv, b0, b1, b2);
+      limbs3(v.z, inv, c0, c1, c2);
+      limbs3(v.w, inv, e0, e1, e2);
+      *reinterpret_cast<uint32_t*>(l0 + k) = pack4(a0, b0, c0, e0);
+      *reinterpret_cast<uint32_t*>(l1 + k) = pack4(a1, b1, c1, e1);
+      *reinterpret_cast<uint32_t*>(l2 + k) = pack4(a2, b2, c2, e2);
+    }
+  } else {
+    for (int64_t k = threadIdx.x; k < K; k += blockDim.x) {
+      int d0, d1, d2;
+      limbs3(xr[k], inv, d0, d1, d2);
+      l0[k] = static_cast<int8_t>(d0);
+      l1[k] = static_cast<int8_t>(d1);
+      l2[k] = static_cast<int8_t>(d2);
+    }
   }
   if (threadIdx.x == 0) sx[m] = s;
 }
