@@ -112,8 +112,10 @@ def mlp_algorithmic_bytes(H, I, ng=1, ngd=1, M=1) -> int:
 #                                                   in lockstep, context 2048
 #   python -m quartz_b200.workloads mlp8b           one Qwen3-8B fused MLP layer
 #                                                   (H 4096, I 12288), 3 calls
-#   python -m quartz_b200.workloads attn8b          decode attention, Qwen3-8B
-#                                                   heads, context 2048, 3 calls
+#   python -m quartz_b200.workloads attn8b [--batch B]
+#                                                   decode attention, Qwen3-8B
+#                                                   heads, context 2048, B
+#                                                   sequences, 3 calls
 #   python -m quartz_b200.workloads prefill         Llama-3.2-1B 512-token prefill
 #
 # --profile-last (decode, decode8b, batch8b, mlp8b, attn8b): the last token /
@@ -142,7 +144,8 @@ def _main(argv=None) -> None:
     b8.add_argument("--batch", type=int, default=16)
     b8.add_argument("--tokens", type=int, default=3)
     sub.add_parser("mlp8b")
-    sub.add_parser("attn8b")
+    a8 = sub.add_parser("attn8b")
+    a8.add_argument("--batch", type=int, default=1)
     sub.add_parser("prefill")
     for p_ in (d, d8, b8):
         p_.add_argument("--profile-last", action="store_true")
@@ -198,22 +201,37 @@ def _main(argv=None) -> None:
         out = profiled(lambda: qd.fused_mlp(gq, gs, x, dq, ds))
         print(f"mlp8b: |out|max {float(out.abs().max()):.4g}")
     elif a.what == "attn8b":
+        import ctypes
+        from . import _lib
         from .model import QWEN3_8B, rope_inv_freq
-        S8 = QWEN3_8B
+        S8, B, T, C = QWEN3_8B, a.batch, 2048, 2112
         gen = torch.Generator(device=dev)
         gen.manual_seed(6)
-        kc = torch.randn(S8.n_kv, 2112, S8.head_dim, device=dev, generator=gen)
-        vc = torch.randn(S8.n_kv, 2112, S8.head_dim, device=dev, generator=gen)
-        qkv = torch.randn(S8.qkv_rows, device=dev, generator=gen)
+        kc = torch.randn(B, S8.n_kv, C, S8.head_dim, device=dev, generator=gen)
+        vc = torch.randn(B, S8.n_kv, C, S8.head_dim, device=dev, generator=gen)
+        qkv = torch.randn(B, S8.qkv_rows, device=dev, generator=gen)
+        out = torch.empty(B, S8.n_heads * S8.head_dim, device=dev)
         inv = torch.from_numpy(rope_inv_freq(S8)).to(dev)
         qn = torch.ones(S8.head_dim, device=dev)
-        pos = torch.tensor([2048], dtype=torch.int64, device=dev)
+        pos = torch.tensor([T], dtype=torch.int64, device=dev)
+        lib = _lib.load()
+        nb = ctypes.c_int64(0)
+        _lib.check(lib.qz_attention_decode_batch_workspace_bytes(
+            B, S8.n_heads, S8.n_kv, S8.head_dim, C, ctypes.byref(nb)))
+        ws = torch.zeros(nb.value, dtype=torch.uint8, device=dev)
+
+        def attn():
+            _lib.check(lib.qz_attention_decode_qkv_batch(
+                qkv.data_ptr(), S8.qkv_rows, qn.data_ptr(), qn.data_ptr(), inv.data_ptr(),
+                kc.data_ptr(), vc.data_ptr(), S8.n_kv * C * S8.head_dim, out.data_ptr(),
+                S8.n_heads * S8.head_dim, B, S8.n_heads, S8.n_kv, S8.head_dim, C, 0,
+                pos.data_ptr(), S8.eps, S8.head_dim ** -0.5, ws.data_ptr(), ws.numel(),
+                torch.cuda.current_stream(dev).cuda_stream))
+            return out
         for _ in range(2):
-            o = qd.attention_decode_qkv(qkv, inv, kc, vc, S8.n_heads, pos_dev=pos, q_norm=qn,
-                                        k_norm=qn)
-        o = profiled(lambda: qd.attention_decode_qkv(qkv, inv, kc, vc, S8.n_heads, pos_dev=pos,
-                                                     q_norm=qn, k_norm=qn))
-        print(f"attn8b: |out|max {float(o.abs().max()):.4g}")
+            attn()
+        o = profiled(attn)
+        print(f"attn8b (batch {B}): |out|max {float(o.abs().max()):.4g}")
     elif a.what == "mlp":
         for l in range(MLP_LAYERS):
             m = mlp_case(MLP_H, MLP_I, seed=MLP_LAYER_SEED0 + l)

@@ -176,3 +176,24 @@ def test_kernel_resources():
     bad = [r for r in rows if r and (int(r.split("smem=")[1].split()[0]) > 256
                                      or int(r.split("spill=")[1]) > 0)]
     assert not bad, bad
+
+
+def test_bench_reference_arm_prints_the_same_config():
+    """`bench.py --impl reference` (the CPU port on the host cores) prints one
+    JSON line whose config is the dict the repo's own arm prints."""
+    import json
+    import subprocess
+    import sys
+    from pathlib import Path
+    repo = Path(__file__).resolve().parent.parent
+    r = subprocess.run([sys.executable, str(repo / "bench.py"), "--impl", "reference", "--steps", "1",
+                        "--warmup", "3"], capture_output=True, text=True, timeout=600, cwd=repo)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [ln for ln in r.stdout.splitlines() if ln.strip()]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    sys.path.insert(0, str(repo))
+    import bench
+    assert d["impl"] == "reference"
+    assert d["config"] == bench.bench_config(1, 3)
+    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["cpu_baseline"]["kind"] == "port"

@@ -203,3 +203,40 @@ def test_tp_shard_eight_kv_heads(world):
         assert lw["model.layers.0.mlp.down_proj"][0].shape == (64, 96 // world)
         assert lq.shape[0] == hi - lo
     assert sum(p[2][3] - p[2][2] for p in parts) == 50
+
+
+def test_seeded_kv_batched_draws():
+    """A batched cache draws [B, n_kv, T, hd] per layer from the same stream
+    (keys then values, layer by layer), as the reference's batched fixtures do;
+    batch=1 is the unbatched draw with a leading axis."""
+    spec = _spec("qwen3_small_kv")
+    one = list(seeded_kv(spec, 7))
+    b1 = list(seeded_kv(spec, 7, batch=1))
+    b3 = list(seeded_kv(spec, 7, batch=3))
+    rng = np.random.default_rng(99)
+    for (k1, v1), (kb1, vb1), (k3, v3) in zip(one, b1, b3):
+        assert kb1.shape == (1,) + k1.shape and np.array_equal(kb1[0], k1)
+        assert np.array_equal(vb1[0], v1)
+        assert k3.shape == (3, spec.n_kv, 7, spec.head_dim)
+        assert np.array_equal(k3, rng.standard_normal(k3.shape, dtype=np.float32))
+        assert np.array_equal(v3, rng.standard_normal(v3.shape, dtype=np.float32))
+
+
+def test_cached_int8_weights_round_trip(tmp_path):
+    """The per-host checkpoint cache returns random_int8_weights' tensors, drawn
+    once and then loaded (writable arrays) from its two flat files."""
+    from quartz_b200.model import cached_int8_weights
+    spec = _spec("qwen3_tiny_kv")
+    want = list(random_int8_weights(spec))
+    first = cached_int8_weights(spec, cache_dir=str(tmp_path))
+    files = sorted(p.name for p in tmp_path.iterdir() if p.suffix == ".npy")
+    assert len(files) == 2
+    again = cached_int8_weights(spec, cache_dir=str(tmp_path))
+    for (n0, q0, s0), (n1, q1, s1), (n2, q2, s2) in zip(want, first, again):
+        assert n0 == n1 == n2
+        assert np.array_equal(q0, q1) and np.array_equal(q0, q2)
+        assert np.array_equal(s0, s1) and np.array_equal(s0, s2)
+        assert q2.flags.writeable and q2.dtype == np.int8 and s2.dtype == np.float32
+    # another seed is another file
+    other = cached_int8_weights(spec, seed=5, cache_dir=str(tmp_path))
+    assert not np.array_equal(other[1][1], want[1][1])
