@@ -596,6 +596,29 @@ __device__ __forceinline__ void norm_rope(float (&x)[E], const float* __restrict
   }
 }
 
+// Sum V values (V a power of two <= 32) over the warp at once: each stage
+// halves the values a lane holds by trading half of them with the lane `o`
+// away, so that afterwards lane l holds the full sum of value l >> log2(32/V)
+// (lanes below that granularity finish with plain butterfly steps). V - 1 +
+// log2(32/V) shuffles instead of 5 V.
+template <int V>
+__device__ __forceinline__ float transpose_sum(float (&v)[V], int lane) {
+#pragma unroll
+  for (int n = V, o = 16; n > 1; n >>= 1, o >>= 1) {
+    const bool up = (lane & o) != 0;
+#pragma unroll
+    for (int i = 0; i < n / 2; ++i) {
+      const float send = up ? v[i] : v[i + n / 2];
+      const float keep = up ? v[i + n / 2] : v[i];
+      v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+    }
+  }
+  float s = v[0];
+#pragma unroll
+  for (int o = 16 / V; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  return s;
+}
+
 // Positions per warp per round of the fused attention: a round's K and V rows
 // are one cp.async group in the warp's private two-round ring.
 template <int E>
@@ -615,9 +638,12 @@ __device__ __forceinline__ void cp_async_lane(uint32_t dst, const float* src) {
 }
 
 template <int E, int NR, bool QKV>
-__global__ void __launch_bounds__(kAttnThreads) attn_decode_fused_kernel(AttnArgs a) {
+__global__ void __launch_bounds__(kAttnThreads, 1) attn_decode_fused_kernel(AttnArgs a) {
   constexpr int HD = 32 * E;
   constexpr int U = attn_round<E>();   // positions per warp per round
+  constexpr int V = U * NR;            // scores per round
+  static_assert(V <= 32 && (V & (V - 1)) == 0, "a round's scores fit one transposed butterfly");
+  constexpr int SH = V == 32 ? 0 : V == 16 ? 1 : V == 8 ? 2 : V == 4 ? 3 : V == 2 ? 4 : 5;
   extern __shared__ float4 attn_smem4[];
   float* qs = reinterpret_cast<float*>(attn_smem4);   // [NR][HD]
   float* red = qs + NR * HD;                           // [warps][NR][HD + 2]
@@ -764,7 +790,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_fused_kernel(AttnArg
           for (int e = 0; e < E; ++e) kr[u][e] = vr[u][e] = 0.f;
         }
       }
-      float sc[U][NR];
+      // The round's U x NR scores: one transposed butterfly sums all of them
+      // over the warp (lane l then holds score v = l >> SH, v = r U + u); the
+      // holders take each head's round maximum among themselves and compute
+      // the softmax numerators, which are then broadcast for the V update.
+      float v[V];
 #pragma unroll
       for (int u = 0; u < U; ++u)
 #pragma unroll
@@ -772,31 +802,39 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_fused_kernel(AttnArg
           float d = 0.f;
 #pragma unroll
           for (int e = 0; e < E; ++e) d = fmaf(q[r][e], kr[u][e], d);
-          sc[u][r] = d;
+          v[r * U + u] = d;
         }
+      const float s_own = transpose_sum<V>(v, lane) * a.scale;
+      const int v_own = lane >> SH;
+      const int r_own = v_own / U, u_own = v_own % U;
+      const bool ok_own =
+          t0 + warp + static_cast<int64_t>(kAttnWarps) * (rd * U + u_own) < t1;
+      float mx = ok_own ? s_own : -INFINITY;
 #pragma unroll
-      for (int u = 0; u < U; ++u)
+      for (int o = 1 << SH; o < (U << SH); o <<= 1)
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      float m_own = m[0];
 #pragma unroll
-        for (int r = 0; r < NR; ++r) sc[u][r] = warp_sum_f(sc[u][r]) * a.scale;
+      for (int r = 1; r < NR; ++r)
+        if (r == r_own) m_own = m[r];
+      // every round's first position exists, so each head's maximum is finite
+      const float mnew_own = fmaxf(m_own, mx);
+      const float p_own = ok_own ? expf(s_own - mnew_own) : 0.f;
 #pragma unroll
       for (int r = 0; r < NR; ++r) {
-        float mx = m[r];
-#pragma unroll
-        for (int u = 0; u < U; ++u)
-          if (ok[u]) mx = fmaxf(mx, sc[u][r]);
-        const float corr = expf(m[r] - mx);
+        const float mnew = __shfl_sync(0xffffffffu, mnew_own, (r * U) << SH);
+        const float corr = expf(m[r] - mnew);
         l[r] *= corr;
 #pragma unroll
         for (int e = 0; e < E; ++e) acc[r][e] *= corr;
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-          if (!ok[u]) continue;
-          const float p = expf(sc[u][r] - mx);
-          l[r] += p;
+          const float pu = __shfl_sync(0xffffffffu, p_own, (r * U + u) << SH);
+          l[r] += pu;
 #pragma unroll
-          for (int e = 0; e < E; ++e) acc[r][e] = fmaf(p, vr[u][e], acc[r][e]);
+          for (int e = 0; e < E; ++e) acc[r][e] = fmaf(pu, vr[u][e], acc[r][e]);
         }
-        m[r] = mx;
+        m[r] = mnew;
       }
     }
     cp_async_wait<0>();
