@@ -99,9 +99,32 @@ __device__ __forceinline__ void cp_async_wait() {
 // COHERENT: the source was written earlier in this kernel by other CTAs (the
 // fused MLP's intermediate, read after the grid barrier): read it from L2
 // (ld.global.cg), never through the non-coherent path.
+// Four consecutive activations 4q .. 4q + 3 land in four consecutive words,
+// so a 16-byte aligned x is staged with float4 loads (four in flight per
+// thread) and one float4 store each.
 template <bool COHERENT = false>
 __device__ __forceinline__ void stage_x(float* xs, const float* x, int64_t K, int tid, int nthr) {
   const int64_t nch = K / 16;
+  if ((reinterpret_cast<uintptr_t>(x) & 15u) == 0) {
+    const int64_t nq = K / 4;      // K % 16 == 0 on the streaming path
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    int64_t q = tid;
+    for (; q + 3 * nthr < nq; q += 4 * nthr) {
+      float4 v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = COHERENT ? __ldcg(x4 + q + u * nthr) : x4[q + u * nthr];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int64_t qq = q + u * nthr;
+        *reinterpret_cast<float4*>(xs + (((qq & 3) * nch) + (qq >> 2)) * 4) = v[u];
+      }
+    }
+    for (; q < nq; q += nthr) {
+      const float4 v = COHERENT ? __ldcg(x4 + q) : x4[q];
+      *reinterpret_cast<float4*>(xs + (((q & 3) * nch) + (q >> 2)) * 4) = v;
+    }
+    return;
+  }
   for (int64_t i = tid; i < K; i += nthr) {
     const int64_t c = i >> 4, j = i & 15;
     xs[((j >> 2) * nch + c) * 4 + (j & 3)] = COHERENT ? __ldcg(x + i) : x[i];
