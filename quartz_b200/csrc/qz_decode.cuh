@@ -464,14 +464,38 @@ __global__ void __launch_bounds__(256) attn_prefill_kernel(
 // take part; sync() is their barrier; scratch holds 2 NR S + NR floats. Two
 // dependent rounds of L2 loads: all maxima and sums at once, then the
 // accumulators, whose loads are independent of one another so they overlap.
-template <int HD, int NR, int NT, class Sync>
+// Splits whose partial accumulators the merge holds in registers.
+constexpr int kMergeRegs = 32;
+
+// REGS: with at most kMergeRegs splits and two outputs per thread, every
+// thread loads its outputs' partial accumulators together with the maxima and
+// sums, one round of L2 loads instead of one per eight splits (off in callers
+// whose register budget is tight).
+template <int HD, int NR, int NT, class Sync, bool REGS = true>
 __device__ __forceinline__ void merge_partials(const float* part_g, int S, float* out_g,
                                                float* scratch, int tid, Sync&& sync) {
   constexpr int NW = NT / 32;
+  constexpr int OPT = (NR * HD + NT - 1) / NT;     // outputs per thread
+  constexpr bool REG = REGS && OPT <= 2;
   const int warp = tid >> 5, lane = tid & 31;
   float* wf = scratch;                // [NR][S] maxima, then weights
   float* lf = scratch + NR * S;       // [NR][S] sums
   float* dn = scratch + 2 * NR * S;   // [NR]
+  constexpr int64_t stride = static_cast<int64_t>(NR) * (HD + 2);
+  float acc_v[REG ? OPT : 1][kMergeRegs];
+  if constexpr (REG) {
+    if (S <= kMergeRegs) {
+#pragma unroll
+      for (int k = 0; k < OPT; ++k) {
+        const int i = tid + k * NT;
+        const int r = i / HD, d = i - r * HD;
+        const float* pr = part_g + r * (HD + 2) + d;
+#pragma unroll
+        for (int c = 0; c < kMergeRegs; ++c)
+          acc_v[k][c] = (i < NR * HD && c < S) ? __ldcg(pr + c * stride) : 0.f;
+      }
+    }
+  }
   for (int i = tid; i < NR * S; i += NT) {
     const int r = i / S, c = i - r * S;
     const float* pr = part_g + (static_cast<int64_t>(c) * NR + r) * (HD + 2) + HD;
@@ -494,7 +518,23 @@ __device__ __forceinline__ void merge_partials(const float* part_g, int S, float
     if (lane == 0) dn[r] = den;
   }
   sync();
-  constexpr int64_t stride = static_cast<int64_t>(NR) * (HD + 2);
+  if constexpr (REG) {
+    if (S <= kMergeRegs) {
+#pragma unroll
+      for (int k = 0; k < OPT; ++k) {
+        const int i = tid + k * NT;
+        if (i >= NR * HD) continue;
+        const int r = i / HD, d = i - r * HD;
+        const float* w = wf + r * S;
+        float num = 0.f;
+#pragma unroll
+        for (int c = 0; c < kMergeRegs; ++c)
+          if (c < S) num = fmaf(w[c], acc_v[k][c], num);
+        out_g[r * HD + d] = num / dn[r];
+      }
+      return;
+    }
+  }
   for (int i = tid; i < NR * HD; i += NT) {
     const int r = i / HD, d = i - r * HD;
     const float* pr = part_g + r * (HD + 2) + d;

@@ -370,10 +370,10 @@ __device__ __forceinline__ void merge_group(const float* part_g, int S, int NR, 
                                             float* scratch, int tid) {
   auto sync = [] { consumer_sync(); };
   switch (NR) {
-    case 1: dec::merge_partials<HD, 1, kConsumers>(part_g, S, out_g, scratch, tid, sync); break;
-    case 2: dec::merge_partials<HD, 2, kConsumers>(part_g, S, out_g, scratch, tid, sync); break;
-    case 4: dec::merge_partials<HD, 4, kConsumers>(part_g, S, out_g, scratch, tid, sync); break;
-    default: dec::merge_partials<HD, 8, kConsumers>(part_g, S, out_g, scratch, tid, sync); break;
+    case 1: dec::merge_partials<HD, 1, kConsumers, decltype(sync)&, false>(part_g, S, out_g, scratch, tid, sync); break;
+    case 2: dec::merge_partials<HD, 2, kConsumers, decltype(sync)&, false>(part_g, S, out_g, scratch, tid, sync); break;
+    case 4: dec::merge_partials<HD, 4, kConsumers, decltype(sync)&, false>(part_g, S, out_g, scratch, tid, sync); break;
+    default: dec::merge_partials<HD, 8, kConsumers, decltype(sync)&, false>(part_g, S, out_g, scratch, tid, sync); break;
   }
 }
 

@@ -339,7 +339,11 @@ __device__ __forceinline__ void norm_staged_x(float* xs, const float* __restrict
                                               float eps, int tid, int nthr) {
   __shared__ float red[32];
   float ss = 0.f;
-  for (int64_t i = tid; i < K; i += nthr) ss = fmaf(xs[i], xs[i], ss);
+  const float4* xs4 = reinterpret_cast<const float4*>(xs);   // K % 16 == 0
+  for (int64_t q = tid; q < K / 4; q += nthr) {
+    const float4 v = xs4[q];
+    ss = fmaf(v.x, v.x, fmaf(v.y, v.y, fmaf(v.z, v.z, fmaf(v.w, v.w, ss))));
+  }
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
   if ((tid & 31) == 0) red[tid >> 5] = ss;
@@ -348,10 +352,19 @@ __device__ __forceinline__ void norm_staged_x(float* xs, const float* __restrict
   for (int i = 0; i < (nthr >> 5); ++i) ss += red[i];
   const float r = 1.0f / sqrtf(ss / static_cast<float>(K) + eps);
   const int64_t nch = K / 16;
-  for (int64_t i = tid; i < K; i += nthr) {
-    const int64_t c = i >> 4, j = i & 15;
-    float& v = xs[((j >> 2) * nch + c) * 4 + (j & 3)];
-    v = v * r * w[i];
+  if ((reinterpret_cast<uintptr_t>(w) & 15u) == 0) {
+    // activations 4q .. 4q + 3 sit in four consecutive words (see stage_x)
+    for (int64_t q = tid; q < K / 4; q += nthr) {
+      float4& v = *reinterpret_cast<float4*>(xs + (((q & 3) * nch) + (q >> 2)) * 4);
+      const float4 wv = reinterpret_cast<const float4*>(w)[q];
+      v = make_float4(v.x * r * wv.x, v.y * r * wv.y, v.z * r * wv.z, v.w * r * wv.w);
+    }
+  } else {
+    for (int64_t i = tid; i < K; i += nthr) {
+      const int64_t c = i >> 4, j = i & 15;
+      float& v = xs[((j >> 2) * nch + c) * 4 + (j & 3)];
+      v = v * r * w[i];
+    }
   }
   __syncthreads();
 }
