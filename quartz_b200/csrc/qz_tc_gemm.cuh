@@ -11,9 +11,10 @@
 //   x[m, k] ~= s_m * (d2 * 2^16 + d1 * 2^8 + d0),   |d2*2^16 + d1*2^8 + d0| <= 2^23 - 2^16
 //
 // i.e. a 24-bit fixed-point copy of each activation row (error <= s_m / 2 =
-// max|x_m| * 2^-24 per element). Each limb is an int8 x int8 MMA
-// (tcgen05.mma kind::i8) accumulating exactly in int32 in tensor memory, so the
-// only rounding is that of the activation split and of the final fp32 scale.
+// max|x_m| * 2^-24 per element). The three limb tiles of a stage form one
+// int8 B operand of 3 * MT rows (tcgen05.mma kind::i8), accumulating exactly in
+// int32 in tensor memory, so the only rounding is that of the activation split
+// and of the final fp32 scale.
 // The weights are never widened and never written back.
 //
 // Operand roles are swapped: the MMA's 128-row "A" operand is a tile of 128
@@ -264,6 +265,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int QB = kRows * kKBytes;       // weight tile bytes
   constexpr int XB = MT * kKBytes;          // one limb tile bytes
   constexpr int SB = QB + kLimbs * XB;
+  // The three limb tiles lie back to back in the stage, so together they are
+  // one K-major B operand of 3 * MT rows: one MMA of N = 3 * MT covers every
+  // limb (N <= 256), two of N = 3 * MT / 2 at MT = 128. TMEM column j of the
+  // accumulator is then limb j / MT, token j % MT, as the epilogue reads it.
+  // (Three MMAs of N = MT per K step measured slower at small MT: the MMA
+  // chain, not the copies, set the stage rate.)
+  constexpr int kMmaPerK = kLimbs * MT <= 256 ? 1 : 2;
+  constexpr int kMmaN = kLimbs * MT / kMmaPerK;
+  static_assert(kMmaN % 16 == 0 && kMmaN <= 256, "MMA N for M = 128");
   uint8_t* tiles = smem;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S * SB);
   const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * kMaxStages;
@@ -335,7 +345,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_i8(MT);
+      constexpr uint32_t idesc = idesc_i8(kMmaN);
       int done = 0;
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % S;
@@ -350,9 +360,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kk = 0; kk < kKBytes / kMmaK; ++kk) {
           const uint64_t ad = smem_desc_sw128(st + kk * kMmaK);
 #pragma unroll
-          for (int l = 0; l < kLimbs; ++l) {
-            const uint64_t bd = smem_desc_sw128(st + QB + l * XB + kk * kMmaK);
-            mma_i8(tmem + l * MT, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
+          for (int h = 0; h < kMmaPerK; ++h) {
+            const uint64_t bd = smem_desc_sw128(st + QB + h * kMmaN * kKBytes + kk * kMmaK);
+            mma_i8(tmem + h * kMmaN, ad, bd, idesc, (kb | kk) != 0 ? 1u : 0u);
           }
         }
         tc_commit(empty0 + 8 * s);   // frees the stage once these MMAs have read it
