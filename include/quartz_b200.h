@@ -118,6 +118,32 @@ int qz_gemm_w8_ws(const int8_t* q, const float* scale, int64_t ng, const float* 
                   int64_t M, int64_t N, int64_t K, const float* residual, void* workspace,
                   size_t workspace_bytes, void* stream);
 
+/* Activation prologues of qz_gemm_w8_act_ws. */
+#define QZ_ACT_NONE 0
+#define QZ_ACT_RMSNORM 1
+#define QZ_ACT_SILU_MUL 2
+
+/*
+ * qz_gemm_w8_ws on an activation computed inside the GEMM's limb split, so
+ * the op that produces the GEMM's input needs no kernel of its own:
+ *   QZ_ACT_RMSNORM   the rows are RMSNorm(X[m, :K]) with weight norm_w [K] and
+ *                    eps (quartz/ops.py:24-32), X is [M, K];
+ *   QZ_ACT_SILU_MUL  the rows are silu(g) * u with the clipped exp of
+ *                    quartz/quantize.py:112-114, X is [M, 2K] holding [g | u];
+ *   QZ_ACT_NONE      qz_gemm_w8_ws itself.
+ * The activations equal what qz_rmsnorm / qz_silu_mul write (same
+ * expressions, same order of the RMSNorm sum), so the result equals the
+ * unfused sequence. Needs the tensor path: M >= 2, ng == 1, K % 16 == 0,
+ * 16-byte aligned q and the workspace of qz_gemm_w8_workspace_bytes;
+ * otherwise QZ_ERR_UNSUPPORTED and nothing is queued. Replaces the RMSNorm +
+ * matmul_int8 and silu-mul + matmul_int8 pairs of quartz's batched decode
+ * (quartz/models/common.py:79-88, quartz/quantize.py:112-114).
+ */
+int qz_gemm_w8_act_ws(const int8_t* q, const float* scale, int64_t ng, const float* X, int act,
+                      const float* norm_w, float eps, float* Y, int64_t M, int64_t N, int64_t K,
+                      const float* residual, void* workspace, size_t workspace_bytes,
+                      void* stream);
+
 /*
  * out[h] = sum down[h, :] * abuf * down_s  (+ residual[h]),
  *   abuf[n] = silu(gate_n . x) * (up_n . x)     (silu with unclipped exp)

@@ -18,6 +18,8 @@ QZ_ERR_CUDA = 2
 QZ_ERR_UNSUPPORTED = 3
 
 # Every symbol include/quartz_b200.h declares, with its ctypes signature.
+# activation prologues of qz_gemm_w8_act_ws (include/quartz_b200.h)
+QZ_ACT_NONE, QZ_ACT_RMSNORM, QZ_ACT_SILU_MUL = 0, 1, 2
 _vp = ctypes.c_void_p
 _i64 = ctypes.c_int64
 _int = ctypes.c_int
@@ -34,6 +36,8 @@ SIGNATURES = {
     "qz_gemm_w8_workspace_bytes": ([_i64, _i64, _i64, ctypes.POINTER(_i64)], _int),
     "qz_gemm_w8_ws": ([_vp, _vp, _i64, _vp, _vp, _i64, _i64, _i64, _vp, _vp, ctypes.c_size_t, _vp],
                       _int),
+    "qz_gemm_w8_act_ws": ([_vp, _vp, _i64, _vp, _int, _vp, ctypes.c_float, _vp, _i64, _i64, _i64,
+                           _vp, _vp, ctypes.c_size_t, _vp], _int),
     "qz_mlp_workspace_bytes": ([], _int),
     "qz_fused_mlp_decode_noalloc": ([_vp, _vp, _i64, _vp, _vp, _vp, _i64, _vp, _vp, _i64, _i64,
                                      _vp], _int),

@@ -442,7 +442,8 @@ int launch_tc(const DeviceInfo& d, const CUtensorMap& tq, const CUtensorMap& tx,
 
 int tc_gemm(const DeviceInfo& d, const int8_t* q, const float* scale, const float* X, float* Y,
             int64_t M, int64_t N, int64_t K, const float* residual, void* ws, size_t ws_bytes,
-            cudaStream_t st) {
+            cudaStream_t st, int act = qz::tc::kActNone, const float* norm_w = nullptr,
+            float eps = 0.f) {
   const TcLayout L = tc_layout(M, N, K);
   int8_t* limbs = static_cast<int8_t*>(ws);
   float* sx = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + L.limb_bytes);
@@ -450,8 +451,20 @@ int tc_gemm(const DeviceInfo& d, const int8_t* q, const float* scale, const floa
                      ? reinterpret_cast<int32_t*>(static_cast<uint8_t*>(ws) + L.limb_bytes +
                                                   L.sx_bytes)
                      : nullptr;
-  qz::tc::split_x_kernel<<<static_cast<unsigned>(L.mpad), qz::tc::kSplitThreads, 0, st>>>(
-      X, limbs, sx, M, L.mpad, K);
+  const dim3 sgrid(static_cast<unsigned>(L.mpad));
+  switch (act) {
+    case qz::tc::kActRmsNorm:
+      qz::tc::split_x_kernel<qz::tc::kActRmsNorm><<<sgrid, qz::tc::kSplitThreads, 0, st>>>(
+          X, K, norm_w, eps, limbs, sx, M, L.mpad, K);
+      break;
+    case qz::tc::kActSiluMul:
+      qz::tc::split_x_kernel<qz::tc::kActSiluMul><<<sgrid, qz::tc::kSplitThreads, 0, st>>>(
+          X, 2 * K, nullptr, 0.f, limbs, sx, M, L.mpad, K);
+      break;
+    default:
+      qz::tc::split_x_kernel<qz::tc::kActNone><<<sgrid, qz::tc::kSplitThreads, 0, st>>>(
+          X, K, nullptr, 0.f, limbs, sx, M, L.mpad, K);
+  }
   QZ_CUDA(cudaGetLastError());
   CUtensorMap tq, tx;
   if (int rc = make_tmap_u8(&tq, q, N, K, qz::tc::kRows)) return rc;
@@ -630,6 +643,37 @@ int qz_gemm_w8_ws(const int8_t* q, const float* scale, int64_t ng, const float* 
                       static_cast<int64_t>(workspace_bytes) >= L.limb_bytes + L.sx_bytes;
   if (!tensor) return launch_generic_gemm(*d, q, scale, ng, X, Y, residual, M, N, K, st);
   return tc_gemm(*d, q, scale, X, Y, M, N, K, residual, workspace, workspace_bytes, st);
+}
+
+int qz_gemm_w8_act_ws(const int8_t* q, const float* scale, int64_t ng, const float* X, int act,
+                      const float* norm_w, float eps, float* Y, int64_t M, int64_t N, int64_t K,
+                      const float* residual, void* workspace, size_t workspace_bytes,
+                      void* stream) {
+  if (act == QZ_ACT_NONE)
+    return qz_gemm_w8_ws(q, scale, ng, X, Y, M, N, K, residual, workspace, workspace_bytes,
+                         stream);
+  if (act != QZ_ACT_RMSNORM && act != QZ_ACT_SILU_MUL)
+    return fail(QZ_ERR_INVALID, "qz_gemm_w8_act_ws: unknown act");
+  if (int rc = check_weights(q, scale, ng, N, K, "qz_gemm_w8_act_ws")) return rc;
+  if (M < 0) return fail(QZ_ERR_INVALID, "qz_gemm_w8_act_ws: negative M");
+  if (M == 0 || N == 0) return QZ_OK;
+  if (!Y || !X || K < 1) return fail(QZ_ERR_INVALID, "qz_gemm_w8_act_ws: null X or Y, or K < 1");
+  if (act == QZ_ACT_RMSNORM && !norm_w)
+    return fail(QZ_ERR_INVALID, "qz_gemm_w8_act_ws: RMSNorm needs norm_w");
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  const TcLayout L = tc_layout(M, N, K);
+  // only the tensor path has a split kernel to carry the prologue
+  const bool tensor = M >= 2 && ng == 1 && K % 16 == 0 && aligned16(q) && workspace &&
+                      aligned16(workspace) &&
+                      static_cast<int64_t>(workspace_bytes) >= L.limb_bytes + L.sx_bytes;
+  if (!tensor)
+    return fail(QZ_ERR_UNSUPPORTED,
+                "qz_gemm_w8_act_ws: needs M >= 2, per-row scales, K % 16 == 0, aligned weights "
+                "and the limb workspace");
+  return tc_gemm(*d, q, scale, X, Y, M, N, K, residual, workspace, workspace_bytes,
+                 static_cast<cudaStream_t>(stream),
+                 act == QZ_ACT_RMSNORM ? qz::tc::kActRmsNorm : qz::tc::kActSiluMul, norm_w, eps);
 }
 
 int qz_mlp_workspace_bytes(void) { return 256; }
@@ -913,16 +957,17 @@ struct AttnLayout {
   int64_t part_off, q_off, total;
 };
 
-// Context splits per kv head: about one CTA per SM in all (more splits cost
-// more in the merge than they gain: 19 vs 24 us at Qwen3-8B shapes, context
-// 2048), at least 32 positions per split, at most 32: the last CTA of a kv
-// head merges the splits' partials in rounds of dependent L2 loads, so a
-// tensor-parallel rank with one or two kv heads would otherwise spend more
-// on the merge (66 splits at one kv head and context 2112) than on its
-// share of the cache.
+// Context splits per kv head: about two CTAs per SM in all, at least 32
+// positions per split, at most 32. Since the merge loads every split's
+// partials in one round, two CTAs per SM beat one (Qwen3-8B heads, context
+// 2048, graph replay: 11.5 vs 12.7 us); before that change one was faster.
+// The cap: the last CTA of a kv head merges the splits' partials from L2, so
+// a tensor-parallel rank with one or two kv heads would otherwise spend more
+// on the merge (66 splits at one kv head and context 2112) than on its share
+// of the cache.
 constexpr int kMaxAttnSplits = 32;
 int attn_splits(const DeviceInfo& d, int nkv, int64_t max_ctx) {
-  const int64_t s = std::min<int64_t>(std::min<int64_t>(qz::cdiv(d.sms, nkv),
+  const int64_t s = std::min<int64_t>(std::min<int64_t>(qz::cdiv(2 * int64_t(d.sms), nkv),
                                                          qz::cdiv(max_ctx, 32)), kMaxAttnSplits);
   return static_cast<int>(std::max<int64_t>(1, s));
 }
@@ -1117,12 +1162,14 @@ int qz_attention_decode_qkv(const float* qkv, const float* q_norm_w, const float
 
 namespace {
 // Batched decode attention: context splits per (sequence, kv head) so that
-// all sequences together put about six CTAs on every SM (enough loads in
-// flight to stream the caches), never more than one sequence alone uses.
+// all sequences together put about three CTAs on every SM (two resident at a
+// time), never more than one sequence alone uses. Same-box sweep of the
+// multiplier (2, 3, 4, 6, 8, 12 CTAs per SM) at Qwen3-8B heads, context 2048:
+// 3 was fastest at 4, 8 and 16 sequences (16: 56.3 us vs 61.8 at 6).
 int attn_splits_batch(const DeviceInfo& d, int nkv, int64_t max_ctx, int batch) {
   const int one = attn_splits(d, nkv, max_ctx);
   if (batch <= 1) return one;
-  const int64_t s = qz::cdiv(int64_t(6) * d.sms, int64_t(nkv) * batch);
+  const int64_t s = qz::cdiv(int64_t(3) * d.sms, int64_t(nkv) * batch);
   return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(s, one)));
 }
 

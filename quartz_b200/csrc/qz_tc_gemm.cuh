@@ -76,9 +76,61 @@ __device__ __forceinline__ uint32_t pack4(int a, int b, int c, int d) {
          ((static_cast<uint32_t>(c) & 255u) << 16) | ((static_cast<uint32_t>(d) & 255u) << 24);
 }
 
-// K % 4 == 0 and 16-byte aligned rows: float4 loads, one 4-byte store per
+// What the split kernel applies to each activation row before splitting it,
+// so that the op producing the GEMM's input needs no launch of its own:
+//   kActNone     x
+//   kActRmsNorm  x / sqrt(mean(x^2) + eps) * w        (quartz/ops.py:24-32)
+//   kActSiluMul  silu(g) * u of a [g | u] row of 2K    (quartz/quantize.py:112-114)
+// The values are computed with the same expressions and, for the RMSNorm, the
+// same order of the sum of squares (512 threads, thread t adding elements
+// t, t + 512, ... in turn, then warp and block sums) as dec::rmsnorm_kernel
+// and silu_mul_kernel, so they equal what those kernels write.
+constexpr int kActNone = 0, kActRmsNorm = 1, kActSiluMul = 2;
+
+struct SplitAct {
+  const float* w;   // RMSNorm weight [K]
+  float r;          // RMSNorm 1 / rms of the row
+  int64_t K;
+};
+
+template <int ACT>
+__device__ __forceinline__ float act1(const float* xr, const SplitAct& p, int64_t k) {
+  if constexpr (ACT == kActRmsNorm) {
+    return xr[k] * p.r * p.w[k];
+  } else if constexpr (ACT == kActSiluMul) {
+    const float g = xr[k], u = xr[p.K + k];
+    const float c = fminf(fmaxf(g, -88.0f), 88.0f);
+    return g * (1.0f / (1.0f + expf(-c))) * u;
+  } else {
+    return xr[k];
+  }
+}
+
+template <int ACT>
+__device__ __forceinline__ float4 act4(const float* xr, const SplitAct& p, int64_t k) {
+  float4 v = *reinterpret_cast<const float4*>(xr + k);
+  if constexpr (ACT == kActRmsNorm) {
+    const float4 w = *reinterpret_cast<const float4*>(p.w + k);
+    v = make_float4(v.x * p.r * w.x, v.y * p.r * w.y, v.z * p.r * w.z, v.w * p.r * w.w);
+  } else if constexpr (ACT == kActSiluMul) {
+    const float4 u = *reinterpret_cast<const float4*>(xr + p.K + k);
+    auto sm = [](float g, float uu) {
+      const float c = fminf(fmaxf(g, -88.0f), 88.0f);
+      return g * (1.0f / (1.0f + expf(-c))) * uu;
+    };
+    v = make_float4(sm(v.x, u.x), sm(v.y, u.y), sm(v.z, u.z), sm(v.w, u.w));
+  }
+  return v;
+}
+
+// One CTA per (padded) activation row; rows are ldx floats apart. K % 4 == 0
+// and 16-byte aligned rows (and weights): float4 loads, one 4-byte store per
 // limb per 4 activations; otherwise element by element.
+template <int ACT>
 __global__ void __launch_bounds__(kSplitThreads) split_x_kernel(const float* __restrict__ X,
+                                                                int64_t ldx,
+                                                                const float* __restrict__ norm_w,
+                                                                float eps,
                                                                 int8_t* __restrict__ limbs,
                                                                 float* __restrict__ sx, int64_t M,
                                                                 int64_t Mpad, int64_t K) {
@@ -91,18 +143,32 @@ __global__ void __launch_bounds__(kSplitThreads) split_x_kernel(const float* __r
     if (threadIdx.x == 0) sx[m] = 0.f;
     return;
   }
-  const float* xr = X + m * K;
-  const bool vec = (K & 3) == 0 && (reinterpret_cast<uintptr_t>(xr) & 15u) == 0;
+  const float* xr = X + m * ldx;
+  __shared__ float red[kSplitThreads / 32];
+  SplitAct p{norm_w, 1.0f, K};
+  if constexpr (ACT == kActRmsNorm) {
+    float ss = 0.f;
+    for (int64_t i = threadIdx.x; i < K; i += blockDim.x) ss = fmaf(xr[i], xr[i], ss);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float t = 0.f;
+    for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) t += red[w];
+    p.r = 1.0f / sqrtf(t / static_cast<float>(K) + eps);
+    __syncthreads();   // red is reused below
+  }
+  bool vec = (K & 3) == 0 && (reinterpret_cast<uintptr_t>(xr) & 15u) == 0;
+  if constexpr (ACT == kActRmsNorm) vec = vec && (reinterpret_cast<uintptr_t>(norm_w) & 15u) == 0;
   float mx = 0.f;
   if (vec) {
     for (int64_t k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
-      const float4 v = *reinterpret_cast<const float4*>(xr + k);
+      const float4 v = act4<ACT>(xr, p, k);
       mx = fmaxf(mx, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
     }
   } else {
-    for (int64_t k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(xr[k]));
+    for (int64_t k = threadIdx.x; k < K; k += blockDim.x) mx = fmaxf(mx, fabsf(act1<ACT>(xr, p, k)));
   }
-  __shared__ float red[kSplitThreads / 32];
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
@@ -113,7 +179,7 @@ __global__ void __launch_bounds__(kSplitThreads) split_x_kernel(const float* __r
   const float inv = 1.0f / s;
   if (vec) {
     for (int64_t k = threadIdx.x * 4; k < K; k += blockDim.x * 4) {
-      const float4 v = *reinterpret_cast<const float4*>(xr + k);
+      const float4 v = act4<ACT>(xr, p, k);
       int a0, a1, a2, b0, b1, b2, c0, c1, c2, e0, e1, e2;
       limbs3(v.x, inv, a0, a1, a2);
       limbs3(v.y, inv, b0, b1, b2);
@@ -126,7 +192,7 @@ __global__ void __launch_bounds__(kSplitThreads) split_x_kernel(const float* __r
   } else {
     for (int64_t k = threadIdx.x; k < K; k += blockDim.x) {
       int d0, d1, d2;
-      limbs3(xr[k], inv, d0, d1, d2);
+      limbs3(act1<ACT>(xr, p, k), inv, d0, d1, d2);
       l0[k] = static_cast<int8_t>(d0);
       l1[k] = static_cast<int8_t>(d1);
       l2[k] = static_cast<int8_t>(d2);

@@ -393,16 +393,37 @@ class DecodeEngine:
         chk(lib.qz_argmax(p(self.logits), 1, S.vocab, p(self.keys), p(self.tok), p(self.pos_dev),
                           1, st))
 
+    def _gemm_act(self, q, s, x: int, act: int, norm_w: int | None, y: int, M: int, N: int,
+                  K: int, residual: int | None, st: int) -> None:
+        """The int8 GEMM of M > 1 rows on an activation of x: its RMSNorm
+        (act QZ_ACT_RMSNORM, weight norm_w) or silu(g) * u of its [g | u] rows
+        (QZ_ACT_SILU_MUL). With fold_norms and a tensor-path shape the
+        activation is computed inside the GEMM's limb split (one kernel less);
+        otherwise qz_rmsnorm / qz_silu_mul write it first. Both give the same
+        values."""
+        lib, chk = self.lib, _lib.check
+        ws, wsb = self.gemm_ws.data_ptr(), self.gemm_ws.numel()
+        if self.fold_norms and s.shape[1] == 1 and K % 16 == 0:
+            chk(lib.qz_gemm_w8_act_ws(q.data_ptr(), s.data_ptr(), 1, x, act, norm_w,
+                                      self.spec.eps, y, M, N, K, residual, ws, wsb, st))
+            return
+        if act == _lib.QZ_ACT_RMSNORM:
+            chk(lib.qz_rmsnorm(x, norm_w, self.xn.data_ptr(), M, K, self.spec.eps, st))
+            src = self.xn.data_ptr()
+        else:
+            chk(lib.qz_silu_mul(x, self.act.data_ptr(), M, K, st))
+            src = self.act.data_ptr()
+        chk(lib.qz_gemm_w8_ws(q.data_ptr(), s.data_ptr(), s.shape[1], src, y, M, N, K, residual,
+                              ws, wsb, st))
+
     def _batch_layer_attn(self, li: int, L, st: int) -> None:
         """RMSNorm, q/k/v GEMM and the batched attention of layer li for the
         B rows in h_a; the attention output goes to ao."""
         S, lib, chk = self.spec, self.lib, _lib.check
         B, H, hd, nq, nkv = self.batch, S.hidden, S.head_dim, S.n_heads, S.n_kv
         p = lambda t: t.data_ptr()  # noqa: E731
-        ws, wsb = p(self.gemm_ws), self.gemm_ws.numel()
-        chk(lib.qz_rmsnorm(p(self.h_a), p(L.in_w), p(self.xn), B, H, S.eps, st))
-        chk(lib.qz_gemm_w8_ws(p(L.qkv_q), p(L.qkv_s), L.qkv_s.shape[1], p(self.xn), p(self.qkv),
-                              B, S.qkv_rows, H, None, ws, wsb, st))
+        self._gemm_act(L.qkv_q, L.qkv_s, p(self.h_a), _lib.QZ_ACT_RMSNORM, p(L.in_w),
+                       p(self.qkv), B, S.qkv_rows, H, None, st)
         chk(lib.qz_attention_decode_qkv_batch(
             p(self.qkv), self.qkv.shape[1], qd._ptr(L.qn_w), qd._ptr(L.kn_w), p(self.inv_freq),
             p(self.k_cache[li]), p(self.v_cache[li]), nkv * self.max_ctx * hd, p(self.ao),
@@ -417,7 +438,7 @@ class DecodeEngine:
         S, lib, chk = self.spec, self.lib, _lib.check
         B, H, hd, nq, I = self.batch, S.hidden, S.head_dim, S.n_heads, S.inter
         p = lambda t: t.data_ptr()  # noqa: E731
-        h_a, h_b, xn = p(self.h_a), p(self.h_b), p(self.xn)
+        h_a, h_b = p(self.h_a), p(self.h_b)
         ws, wsb = p(self.gemm_ws), self.gemm_ws.numel()
         chk(lib.qz_embed_gather(p(self.embed_q), p(self.embed_s), self.embed_s.shape[1],
                                 p(self.tok), B, S.vocab, H, h_a, st))
@@ -425,16 +446,13 @@ class DecodeEngine:
             self._batch_layer_attn(li, L, st)
             chk(lib.qz_gemm_w8_ws(p(L.o_q), p(L.o_s), L.o_s.shape[1], p(self.ao), h_b, B, H,
                                   nq * hd, h_a, ws, wsb, st))
-            chk(lib.qz_rmsnorm(h_b, p(L.post_w), xn, B, H, S.eps, st))
-            chk(lib.qz_gemm_w8_ws(p(L.gu_q), p(L.gu_s), L.gu_s.shape[1], xn, p(self.gu), B,
-                                  2 * I, H, None, ws, wsb, st))
-            chk(lib.qz_silu_mul(p(self.gu), p(self.act), B, I, st))
-            chk(lib.qz_gemm_w8_ws(p(L.down_q), p(L.down_s), L.down_s.shape[1], p(self.act), h_a,
-                                  B, H, I, h_b, ws, wsb, st))
-        chk(lib.qz_rmsnorm(h_a, p(self.norm_w), xn, B, H, S.eps, st))
+            self._gemm_act(L.gu_q, L.gu_s, h_b, _lib.QZ_ACT_RMSNORM, p(L.post_w), p(self.gu),
+                           B, 2 * I, H, None, st)
+            self._gemm_act(L.down_q, L.down_s, p(self.gu), _lib.QZ_ACT_SILU_MUL, None, h_a,
+                           B, H, I, h_b, st)
         V = self.lm_q.shape[0]
-        chk(lib.qz_gemm_w8_ws(p(self.lm_q), p(self.lm_s), self.lm_s.shape[1], xn,
-                              p(self.logits), B, V, H, None, ws, wsb, st))
+        self._gemm_act(self.lm_q, self.lm_s, h_a, _lib.QZ_ACT_RMSNORM, p(self.norm_w),
+                       p(self.logits), B, V, H, None, st)
         chk(lib.qz_argmax(p(self.logits), B, V, p(self.keys), p(self.tok), p(self.pos_dev), 1,
                           st))
 
@@ -448,14 +466,23 @@ class DecodeEngine:
         tiles = -(-N // 128) * (-(-M // mt))
         return 3 if tiles < sms else 2
 
+    def _prologue_launches(self, s, K: int) -> int:
+        """Launches of the RMSNorm / silu before a GEMM of K columns with
+        scales s: none when _gemm_act computes it inside the limb split."""
+        return 0 if self.fold_norms and s.shape[1] == 1 and K % 16 == 0 else 1
+
     def _launches_per_token(self) -> int:
         if self.batch > 1:
             # per step (B tokens): embed, per layer (rmsnorm, qkv GEMM, attention, o GEMM,
-            # rmsnorm, gate/up GEMM, silu, down GEMM), final rmsnorm, lm_head GEMM, argmax x2
-            S, B, g = self.spec, self.batch, self._gemm_launches
-            per_layer = (4 + g(B, S.qkv_rows) + g(B, S.hidden) + g(B, 2 * S.inter)
-                         + g(B, S.hidden))
-            return 1 + per_layer * S.layers + 1 + g(B, self.lm_q.shape[0]) + 2
+            # rmsnorm, gate/up GEMM, silu, down GEMM), final rmsnorm, lm_head GEMM, argmax x2;
+            # a norm or the silu inside its GEMM's limb split launches nothing of its own
+            S, B, g, pre = self.spec, self.batch, self._gemm_launches, self._prologue_launches
+            L0 = self.layers[0]
+            per_layer = (1 + pre(L0.qkv_s, S.hidden) + g(B, S.qkv_rows) + g(B, S.hidden)
+                         + pre(L0.gu_s, S.hidden) + g(B, 2 * S.inter)
+                         + pre(L0.down_s, S.inter) + g(B, S.hidden))
+            return (1 + per_layer * S.layers + pre(self.lm_s, S.hidden)
+                    + g(B, self.lm_q.shape[0]) + 2)
         if self.persistent:
             return 4   # decode_layers, lm_head GEMV, argmax + finish
         # embed + per layer (qkv with its norm, attention, o, mlp with its norm) + lm with
@@ -502,9 +529,8 @@ class DecodeEngine:
                                 p(self.ids), M, S.vocab, H, h_a, st))
         for li, L in enumerate(self.layers):
             kc, vc = p(self.k_cache[li]), p(self.v_cache[li])
-            chk(lib.qz_rmsnorm(h_a, p(L.in_w), xn, M, H, S.eps, st))
-            chk(lib.qz_gemm_w8_ws(p(L.qkv_q), p(L.qkv_s), L.qkv_s.shape[1], xn, p(self.qkv), M,
-                                  S.qkv_rows, H, None, ws, wsb, st))
+            self._gemm_act(L.qkv_q, L.qkv_s, h_a, _lib.QZ_ACT_RMSNORM, p(L.in_w), p(self.qkv),
+                           M, S.qkv_rows, H, None, st)
             chk(lib.qz_qk_rope(p(self.qkv), qd._ptr(L.qn_w), qd._ptr(L.kn_w), p(self.inv_freq),
                                p(self.qo), kc, vc, M, nq, nkv, hd, self.max_ctx, pos0, None,
                                S.eps, st))
@@ -512,12 +538,10 @@ class DecodeEngine:
                                          self.max_ctx, pos0, self.attn_scale, st))
             chk(lib.qz_gemm_w8_ws(p(L.o_q), p(L.o_s), L.o_s.shape[1], p(self.ao), h_b, M, H,
                                   nq * hd, h_a, ws, wsb, st))
-            chk(lib.qz_rmsnorm(h_b, p(L.post_w), xn, M, H, S.eps, st))
-            chk(lib.qz_gemm_w8_ws(p(L.gu_q), p(L.gu_s), L.gu_s.shape[1], xn, p(self.gu), M,
-                                  2 * I, H, None, ws, wsb, st))
-            chk(lib.qz_silu_mul(p(self.gu), p(self.act), M, I, st))
-            chk(lib.qz_gemm_w8_ws(p(L.down_q), p(L.down_s), L.down_s.shape[1], p(self.act), h_a,
-                                  M, H, I, h_b, ws, wsb, st))
+            self._gemm_act(L.gu_q, L.gu_s, h_b, _lib.QZ_ACT_RMSNORM, p(L.post_w), p(self.gu),
+                           M, 2 * I, H, None, st)
+            self._gemm_act(L.down_q, L.down_s, p(self.gu), _lib.QZ_ACT_SILU_MUL, None, h_a,
+                           M, H, I, h_b, st)
         last = h_a + (M - 1) * H * 4
         chk(lib.qz_rmsnorm(last, p(self.norm_w), xn, 1, H, S.eps, st))
         chk(lib.qz_gemv_w8(p(self.lm_q), p(self.lm_s), self.lm_s.shape[1], xn, p(self.logits),

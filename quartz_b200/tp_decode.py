@@ -236,7 +236,7 @@ class TPDecodeEngine(DecodeEngine):
         S, lib, chk = self.spec, self.lib, _lib.check
         B, H, hd, nq, I = self.batch, S.hidden, S.head_dim, S.n_heads, S.inter
         p = lambda t: t.data_ptr()  # noqa: E731
-        h_a, h_b, xn = p(self.h_a), p(self.h_b), p(self.xn)
+        h_a, h_b = p(self.h_a), p(self.h_b)
         ws, wsb = p(self.gemm_ws), self.gemm_ws.numel()
         first = self.rank == 0
         chk(lib.qz_embed_gather(p(self.embed_q), p(self.embed_s), self.embed_s.shape[1],
@@ -246,18 +246,15 @@ class TPDecodeEngine(DecodeEngine):
             chk(lib.qz_gemm_w8_ws(p(L.o_q), p(L.o_s), L.o_s.shape[1], p(self.ao), h_b, B, H,
                                   nq * hd, h_a if first else None, ws, wsb, st))
             self._all_reduce(self.h_b[:B])
-            chk(lib.qz_rmsnorm(h_b, p(L.post_w), xn, B, H, S.eps, st))
-            chk(lib.qz_gemm_w8_ws(p(L.gu_q), p(L.gu_s), L.gu_s.shape[1], xn, p(self.gu), B,
-                                  2 * I, H, None, ws, wsb, st))
-            chk(lib.qz_silu_mul(p(self.gu), p(self.act), B, I, st))
-            chk(lib.qz_gemm_w8_ws(p(L.down_q), p(L.down_s), L.down_s.shape[1], p(self.act), h_a,
-                                  B, H, I, h_b if first else None, ws, wsb, st))
+            self._gemm_act(L.gu_q, L.gu_s, h_b, _lib.QZ_ACT_RMSNORM, p(L.post_w), p(self.gu),
+                           B, 2 * I, H, None, st)
+            self._gemm_act(L.down_q, L.down_s, p(self.gu), _lib.QZ_ACT_SILU_MUL, None, h_a,
+                           B, H, I, h_b if first else None, st)
             self._all_reduce(self.h_a[:B])
-        chk(lib.qz_rmsnorm(h_a, p(self.norm_w), xn, B, H, S.eps, st))
         n_local = self.vhi - self.vlo
         if n_local > 0:
-            chk(lib.qz_gemm_w8_ws(p(self.lm_q), p(self.lm_s), self.lm_s.shape[1], xn,
-                                  p(self.logits), B, n_local, H, None, ws, wsb, st))
+            self._gemm_act(self.lm_q, self.lm_s, h_a, _lib.QZ_ACT_RMSNORM, p(self.norm_w),
+                           p(self.logits), B, n_local, H, None, st)
         self._pick_token(st, 1)
 
     def _decode_ops(self, st: int) -> None:
@@ -299,6 +296,19 @@ class TPDecodeEngine(DecodeEngine):
         self._pick_token(st, 1)
 
     def _launches_per_token(self) -> int:
+        if self.batch > 1:
+            # per step: embed, per layer (qkv GEMM with its norm, attention, o GEMM,
+            # [peer all-reduce], gate/up GEMM with its norm, down GEMM with the silu,
+            # [peer all-reduce]), lm_head GEMM with the final norm, argmax x2 (NCCL
+            # collectives and the torch ops of the vocab pick are not counted)
+            S, B, g, pre = self.spec, self.batch, self._gemm_launches, self._prologue_launches
+            L0, ar = self.layers[0], int(self.peer is not None)
+            per_layer = (1 + pre(L0.qkv_s, S.hidden) + g(B, S.qkv_rows) + g(B, S.hidden) + ar
+                         + pre(L0.gu_s, S.hidden) + g(B, 2 * S.inter)
+                         + pre(L0.down_s, S.inter) + g(B, S.hidden) + ar)
+            n_local = self.vhi - self.vlo
+            lm = pre(self.lm_s, S.hidden) + g(B, n_local) + 2 if n_local > 0 else 0
+            return 1 + per_layer * S.layers + lm
         if self.fused_ar:
             # embed, rmsnorm + per layer (qkv, attention, o, peer sum, mlp, peer sum) + lm, argmax
             return 2 + 6 * self.spec.layers + 2
@@ -335,9 +345,8 @@ class TPDecodeEngine(DecodeEngine):
                                 p(self.ids), M, S.vocab, H, h_a, st))
         for li, L in enumerate(self.layers):
             kc, vc = p(self.k_cache[li]), p(self.v_cache[li])
-            chk(lib.qz_rmsnorm(h_a, p(L.in_w), xn, M, H, S.eps, st))
-            chk(lib.qz_gemm_w8_ws(p(L.qkv_q), p(L.qkv_s), L.qkv_s.shape[1], xn, p(self.qkv), M,
-                                  S.qkv_rows, H, None, ws, wsb, st))
+            self._gemm_act(L.qkv_q, L.qkv_s, h_a, _lib.QZ_ACT_RMSNORM, p(L.in_w), p(self.qkv),
+                           M, S.qkv_rows, H, None, st)
             chk(lib.qz_qk_rope(p(self.qkv), _ptr(L.qn_w), _ptr(L.kn_w), p(self.inv_freq),
                                p(self.qo), kc, vc, M, nq, nkv, hd, self.max_ctx, pos0, None,
                                S.eps, st))
@@ -346,12 +355,10 @@ class TPDecodeEngine(DecodeEngine):
             chk(lib.qz_gemm_w8_ws(p(L.o_q), p(L.o_s), L.o_s.shape[1], p(self.ao), h_b, M, H,
                                   nq * hd, h_a if first else None, ws, wsb, st))
             self._all_reduce(self.h_b[:M])
-            chk(lib.qz_rmsnorm(h_b, p(L.post_w), xn, M, H, S.eps, st))
-            chk(lib.qz_gemm_w8_ws(p(L.gu_q), p(L.gu_s), L.gu_s.shape[1], xn, p(self.gu), M,
-                                  2 * I, H, None, ws, wsb, st))
-            chk(lib.qz_silu_mul(p(self.gu), p(self.act), M, I, st))
-            chk(lib.qz_gemm_w8_ws(p(L.down_q), p(L.down_s), L.down_s.shape[1], p(self.act), h_a,
-                                  M, H, I, h_b if first else None, ws, wsb, st))
+            self._gemm_act(L.gu_q, L.gu_s, h_b, _lib.QZ_ACT_RMSNORM, p(L.post_w), p(self.gu),
+                           M, 2 * I, H, None, st)
+            self._gemm_act(L.down_q, L.down_s, p(self.gu), _lib.QZ_ACT_SILU_MUL, None, h_a,
+                           M, H, I, h_b if first else None, st)
             self._all_reduce(self.h_a[:M])
         last = h_a + (M - 1) * H * 4
         chk(lib.qz_rmsnorm(last, p(self.norm_w), xn, 1, H, S.eps, st))

@@ -89,3 +89,91 @@ def test_gemm_rows_equal_gemv_rows_tensor_path():
     for m in range(8):
         y = device.gemv(q, s, _t(c.x[m])).cpu().numpy()
         assert np.allclose(Y[m], y, atol=1e-4)
+
+
+def _gemm_ws(M, N, K):
+    import ctypes
+    from quartz_b200 import _lib
+    b = ctypes.c_int64(0)
+    _lib.check(_lib.load().qz_gemm_w8_workspace_bytes(M, N, K, ctypes.byref(b)))
+    return torch.zeros(max(b.value, 256), dtype=torch.uint8, device="cuda")
+
+
+@pytest.mark.parametrize("N,K,M,act", [
+    (3072, 1024, 4, "rmsnorm"),     # Qwen3-0.6B shapes, decode rows: qkv after the input norm
+    (6144, 1024, 16, "rmsnorm"),    # gate|up after the post-attention norm
+    (1024, 3072, 16, "silu"),       # down after silu(gate) * up
+    (2048, 8192, 512, "silu"),      # Llama-1B prefill down
+    (3072, 2048, 512, "rmsnorm"),   # Llama-1B prefill qkv
+    (300, 4112, 3, "rmsnorm"),      # K not a multiple of 128, ragged rows
+    (256, 48, 2, "silu"),           # K below one 512-thread pass
+])
+def test_gemm_activation_prologue_equals_separate_kernels(N, K, M, act):
+    """qz_gemm_w8_act_ws with the RMSNorm or silu(g) * u computed in the
+    GEMM's limb split equals qz_rmsnorm / qz_silu_mul followed by
+    qz_gemm_w8_ws (same activation values, so the same limbs), and both are
+    within the oracle's tolerance of the fp32 reference."""
+    from quartz_b200 import _lib
+    from quartz_b200.workloads import gemv_case
+    lib = _lib.load()
+    st = torch.cuda.current_stream().cuda_stream
+    c = gemv_case(N, K, M, seed=N + 3 * K + M)
+    q, s = _t(c.q), _t(c.scale)
+    rng = np.random.default_rng(K)
+    eps = 1e-6
+    if act == "rmsnorm":
+        X = _t(c.x * 3.0)
+        w = _t(rng.standard_normal(K).astype(np.float32))
+        mid = torch.empty(M, K, device="cuda")
+        _lib.check(lib.qz_rmsnorm(X.data_ptr(), w.data_ptr(), mid.data_ptr(), M, K, eps, st))
+        code, wp = _lib.QZ_ACT_RMSNORM, w.data_ptr()
+    else:
+        X = _t(rng.standard_normal((M, 2 * K)).astype(np.float32) * 4.0)
+        mid = torch.empty(M, K, device="cuda")
+        _lib.check(lib.qz_silu_mul(X.data_ptr(), mid.data_ptr(), M, K, st))
+        code, wp = _lib.QZ_ACT_SILU_MUL, None
+    ws = _gemm_ws(M, N, K)
+    R = _t(rng.standard_normal((M, N)).astype(np.float32))
+    Y_sep = torch.empty(M, N, device="cuda")
+    Y_fused = torch.empty(M, N, device="cuda")
+    _lib.check(lib.qz_gemm_w8_ws(q.data_ptr(), s.data_ptr(), 1, mid.data_ptr(), Y_sep.data_ptr(),
+                                 M, N, K, R.data_ptr(), ws.data_ptr(), ws.numel(), st))
+    for _ in range(2):   # twice: the workspace holds the previous call's limbs
+        _lib.check(lib.qz_gemm_w8_act_ws(q.data_ptr(), s.data_ptr(), 1, X.data_ptr(), code, wp,
+                                         eps, Y_fused.data_ptr(), M, N, K, R.data_ptr(),
+                                         ws.data_ptr(), ws.numel(), st))
+        torch.cuda.synchronize()
+        assert torch.equal(Y_fused, Y_sep), f"{act} {N}x{K} M={M}: fused prologue differs"
+    ref = _oracle_gemm(c.q, c.scale, mid.cpu().numpy()) + R.cpu().numpy()
+    G.assert_close(Y_fused.cpu().numpy(), ref, what=f"{act} {N}x{K} M={M}")
+
+
+def test_gemm_activation_prologue_rejections():
+    """Outside the tensor path (one row, group scales) the prologue entry
+    refuses with QZ_ERR_UNSUPPORTED and queues nothing; an unknown act is an
+    argument error."""
+    from quartz_b200 import _lib
+    from quartz_b200.workloads import gemv_case
+    lib = _lib.load()
+    st = torch.cuda.current_stream().cuda_stream
+    c = gemv_case(256, 1024, 4, seed=5)
+    q, s, X = _t(c.q), _t(c.scale), _t(c.x)
+    w = torch.ones(1024, device="cuda")
+    Y = torch.zeros(4, 256, device="cuda")
+    ws = _gemm_ws(4, 256, 1024)
+    args = (ws.data_ptr(), ws.numel(), st)
+    with pytest.raises(_lib.QuartzError):
+        _lib.check(lib.qz_gemm_w8_act_ws(q.data_ptr(), s.data_ptr(), 1, X.data_ptr(),
+                                         _lib.QZ_ACT_RMSNORM, w.data_ptr(), 1e-6, Y.data_ptr(),
+                                         1, 256, 1024, None, *args))
+    cg = gemv_case(256, 1024, 4, seed=6, group_size=128)
+    with pytest.raises(_lib.QuartzError):
+        _lib.check(lib.qz_gemm_w8_act_ws(_t(cg.q).data_ptr(), _t(cg.scale).data_ptr(), 8,
+                                         X.data_ptr(), _lib.QZ_ACT_RMSNORM, w.data_ptr(), 1e-6,
+                                         Y.data_ptr(), 4, 256, 1024, None, *args))
+    with pytest.raises(ValueError):
+        _lib.check(lib.qz_gemm_w8_act_ws(q.data_ptr(), s.data_ptr(), 1, X.data_ptr(), 7,
+                                         w.data_ptr(), 1e-6, Y.data_ptr(), 4, 256, 1024, None,
+                                         *args))
+    torch.cuda.synchronize()
+    assert float(Y.abs().max()) == 0.0
