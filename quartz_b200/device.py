@@ -41,6 +41,10 @@ def _stream_ptr(dev: torch.device) -> int:
 
 def ensure_device(dev: torch.device | int | None = None) -> int:
     """qz_init once per device (checks that it is an sm_100 GPU)."""
+    if dev is None and _ready_devices:
+        idx = torch.cuda.current_device()   # the per-call path: no availability probe
+        if idx in _ready_devices:
+            return idx
     if not torch.cuda.is_available():
         raise RuntimeError("quartz_b200 needs a CUDA device; none is available")
     if dev is None:

@@ -34,6 +34,17 @@ def _dev_index() -> int:
     return _dev.ensure_device()
 
 
+# The current stream's raw handle without building a torch.cuda.Stream object
+# (a few microseconds a call on the host, which the numpy GEMV pays every call).
+_raw_stream_fn = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _raw_stream(d: int) -> int:
+    if _raw_stream_fn is not None:
+        return _raw_stream_fn(d)
+    return torch.cuda.current_stream(d).cuda_stream
+
+
 def _check_np(q, scale):
     if not isinstance(q, np.ndarray) or q.dtype != np.int8 or q.ndim != 2:
         raise TypeError("q must be a 2-D int8 numpy array")
@@ -73,8 +84,7 @@ def w8a32_gemv(q, scale, x, y) -> None:
     xp, yp, xdv, ydv = _host.io_ptrs(d, 4 * K, 4 * N)
     _lib.check(_lib.load().qz_gemv_w8_host(
         qd.data_ptr(), sd.data_ptr(), scale.shape[1], x.__array_interface__["data"][0],
-        y.__array_interface__["data"][0], N, K, xp, yp, xdv, ydv,
-        torch.cuda.current_stream(d).cuda_stream))
+        y.__array_interface__["data"][0], N, K, xp, yp, xdv, ydv, _raw_stream(d)))
 
 
 def w8a32_gemv_serial(q, scale, x, y) -> None:

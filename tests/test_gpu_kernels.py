@@ -248,3 +248,41 @@ def test_w4a32_gemv_rejects_bad_shapes(K):
     q4 = torch.zeros(8, 24, dtype=torch.uint8, device="cuda")      # K = 48
     with pytest.raises(Exception, match="multiples of 32"):
         device.gemv_w4(q4, torch.ones(8, 1, device="cuda"), torch.ones(48, device="cuda"))
+
+
+def test_numpy_weight_cache_follows_the_arrays():
+    """The numpy entry points keep a device copy of each weight array: the same
+    object hits it without rebuilding its key, a view of the same buffer shares
+    it, invalidate() after an in-place change re-uploads, and the copy is
+    dropped when the array is freed."""
+    import gc
+    from quartz_b200 import _host
+    from quartz_b200.kernels import w8a32_gemv
+    from quartz_b200.workloads import gemv_case
+    c = gemv_case(4096, 1024, seed=11)
+    q, s = c.q.copy(), c.scale.copy()
+    x = c.x[0].copy()
+
+    def ref(qq):
+        y = np.empty(qq.shape[0], np.float32)
+        oracle.w8a32_gemv(qq, s, x, y)
+        return y
+
+    y = np.empty(4096, np.float32)
+    w8a32_gemv(q, s, x, y)
+    G.assert_close(y, ref(q), what="first call")
+    d = torch.cuda.current_device()
+    assert _host.resident(q, d) is _host.resident(q, d)
+    v = q[:]                       # another object over the same buffer
+    assert _host.resident(v, d) is _host.resident(q, d)
+    y2 = np.empty_like(y)
+    w8a32_gemv(v, s, x, y2)
+    assert np.array_equal(y, y2)
+    q[:100] = -q[:100]             # in-place change, announced
+    _host.invalidate(q)
+    w8a32_gemv(q, s, x, y)
+    G.assert_close(y, ref(q), what="after invalidate")
+    before = _host.cached_bytes()
+    del q, v
+    gc.collect()
+    assert _host.cached_bytes() <= before - 4096 * 1024
