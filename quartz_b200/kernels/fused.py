@@ -17,11 +17,12 @@ from .int8 import _check_np, _check_out, _is_torch
 
 
 def fused_mlp_decode(gu_q, gu_s, x, down_q, down_s, abuf, out) -> None:
-    """out[H] = down( silu(gate(x)) * up(x) ), with `x` already RMSNorm'd.
-
-    gu_q:(2*INTER, H) int8 = [gate; up] stacked; gu_s:(2*INTER, ng).
-    down_q:(H, INTER) int8; down_s:(H, ng_d). abuf:(INTER,) written; out:(H,).
-    """
+    """The MLP body of one token on the GPU: for each intermediate unit n,
+    abuf[n] = silu(g_n . x) * (u_n . x), where g_n and u_n are rows n and
+    I + n of the stacked int8 matrix gu_q [2I, H] (scales gu_s [2I, ng]);
+    then out[h] = sum_n down_q[h, n] * abuf[n], scaled by down_s [H, ng_d].
+    x [H] is the already-normalised activation. Both abuf [I] and out [H] are
+    written in place, as in the reference's signature."""
     if _is_torch(gu_q, gu_s, x, down_q, down_s, abuf, out):
         _dev.fused_mlp(gu_q, gu_s, x.reshape(-1), down_q, down_s, abuf, out)
         return

@@ -64,10 +64,10 @@ def _check_out(y, shape, name):
 
 
 def w8a32_gemv(q, scale, x, y) -> None:
-    """Decode GEMV (M=1). q:(N,K) int8; scale:(N,ng) f32; x:(K,) f32; y:(N,) f32 out.
-
-    quartz/kernels/int8.py:24-38. y[n] = sum_g scale[n,g] * sum_j x[gG+j] q[n,gG+j].
-    """
+    """One activation row against int8 weights: y[n] = sum over scale groups g
+    of scale[n, g] * sum_j x[g*G + j] * q[n, g*G + j], with q [N, K] int8,
+    scale [N, ng] float32 (G = K / ng), x [K] and the output y [N] float32,
+    written in place. Same signature as quartz/kernels/int8.py:24-38."""
     if _is_torch(q, scale, x, y):
         _dev.gemv(q, scale, x.reshape(-1), y)
         return
@@ -94,10 +94,9 @@ def w8a32_gemv_serial(q, scale, x, y) -> None:
 
 
 def w8a32_gemm(q, scale, X, Y) -> None:
-    """Prefill GEMM (M>1). q:(N,K) int8; scale:(N,ng) f32; X:(M,K) f32; Y:(M,N) f32 out.
-
-    quartz/kernels/int8.py:66-87.
-    """
+    """Several activation rows at once: Y[m] = the GEMV of X[m] for every m,
+    with X [M, K] and the output Y [M, N] float32 written in place; runs on
+    the tensor cores. Same signature as quartz/kernels/int8.py:66-87."""
     if _is_torch(q, scale, X, Y):
         _dev.gemm(q, scale, X, Y)
         return
