@@ -1192,7 +1192,7 @@ def run_ours(args, rank: int, world: int, local: int) -> dict | None:
     llama = None
     if not args.no_llama and world == 1:
         llama = run_llama_prefill_decode(args, dev)
-    _log(rank, "llama prefill + decode done")
+        _log(rank, "llama prefill + decode done")
     del graphs
 
     if rank != 0:
